@@ -1,0 +1,121 @@
+"""Bit-exact GPU parity of the emulated GEMM (TriCast ``tests/gpu/test_triton_mma.py``) against the
+golden fixtures, all 1,716 NADPE vectors, and the oracle at larger sizes, through the C ABI."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.conftest import bits_equal, first_mismatch
+from tests.golden_cases import bf16_bits, load, mma_operand, mspec, nadpe_cases
+from tricast_b200 import gemm_triton, quantize_triton
+from tricast_b200.formats import FP16, IntFormat
+from tricast_b200.operand import Operand, as_operand
+from tricast_b200.spec import PRESETS, SCHEMES, MMASpec
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a):
+    return None if a is None else torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.float32))).cuda()
+
+
+def cuda_operand(ns) -> Operand:
+    return Operand(_t(ns.values), ns.fmt, _t(ns.scale), ns.scale_fmt, ns.scale_kind, ns.k_domain,
+                   None if ns.alpha is None else _t(np.asarray(ns.alpha, np.float32).reshape(())))
+
+
+@pytest.mark.parametrize("case", load("mma")[0], ids=lambda c: c["id"])
+def test_gemm_golden(case):
+    _, arrays = load("mma")
+    a, b = mma_operand(case, arrays, "a"), mma_operand(case, arrays, "b")
+    spec = mspec(case["spec"])
+    bias = arrays.get(f"{case['id']}|bias")
+    if case["error"] is not None:
+        with pytest.raises(ValueError):
+            gemm_triton(cuda_operand(a), cuda_operand(b), spec, _t(bias))
+        return
+    got = gemm_triton(cuda_operand(a), cuda_operand(b), spec, _t(bias)).float().cpu().numpy()
+    want = arrays[f"{case['id']}|out"]
+    assert got.shape == want.shape
+    assert bits_equal(got, want), f"{spec}: {first_mismatch(got, want)}"
+
+
+def _nadpe_groups():
+    cases = nadpe_cases()
+    return [(k, [c for c in cases if c[0] == k]) for k in sorted({c[0] for c in cases})]
+
+
+@pytest.mark.parametrize("key,cases", _nadpe_groups(), ids=lambda v: v if isinstance(v, str) else "")
+def test_nadpe_vectors_gpu(key, cases):
+    for _, index, a, b, spec, expected in cases:
+        got = gemm_triton(cuda_operand(a), cuda_operand(b), spec)
+        bits = got.contiguous().view(torch.int16).cpu().numpy()
+        assert np.array_equal(bits, expected), f"{key} case {index}: {spec}"
+
+
+def _quantized(scheme, rows, K, seed, scale=1.0, outliers=0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(rows, K, generator=g) * scale
+    if outliers:
+        x[:, torch.randperm(K, generator=g)[:outliers]] *= 20
+    return as_operand(quantize_triton(x.bfloat16().cuda(), SCHEMES[scheme]))
+
+
+def _oracle_gemm(a: Operand, b: Operand, spec):
+    return oracle.gemm_reference(a, b, spec)
+
+
+@pytest.mark.parametrize("scheme,preset", [
+    ("nvfp4", "nvidia_blackwell_fp4"), ("mxfp4", "nvidia_blackwell_fp4"), ("fp8_tensor", "nvidia_hopper_fp8"),
+    ("fp8_tensor", "nvidia_blackwell_fp8"), ("mxfp8_e4m3", "nvidia_hopper_fp8"), ("fp8_tensor", "nvidia_ada_fp8"),
+])
+@pytest.mark.parametrize("out", ["fp32", "bf16"])
+def test_preset_configs_vs_oracle(scheme, preset, out):
+    """Benchmark-config formats and presets at 64x96x1024 against the oracle."""
+    a = _quantized(scheme, 64, 1024, 1, outliers=4)
+    b = _quantized(scheme, 96, 1024, 2, scale=0.02)
+    spec = PRESETS[preset].with_(out_format=out)
+    got = gemm_triton(a, b, spec).float().cpu().numpy()
+    want = _oracle_gemm(a, b, spec)
+    assert bits_equal(got, want), first_mismatch(got, want)
+
+
+def test_cfg4_mapping_vs_oracle():
+    """INT8 row-scaled activations x INT4 g128 asymmetric weights, CoFDA F=23 promoted every 128."""
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(48, 1024, generator=g)
+    w = torch.randn(80, 1024, generator=g) * 0.02
+    qa = quantize_triton(x.cuda(), SCHEMES["int8_row"])
+    qw = quantize_triton(w.cuda(), SCHEMES["int4_g128_zp"])
+    z = qw.zero_point.repeat_interleave(128, dim=1)[:, :1024]
+    a = as_operand(qa)
+    b = Operand(qw.values.float() - z, IntFormat("int5", 5), qw.scale, FP16, "k", 128)
+    spec = MMASpec("cofda", f_bits=23, chunk_size=32, promote_interval=128, out_format="fp32")
+    got = gemm_triton(a, b, spec).cpu().numpy()
+    want = _oracle_gemm(a, b, spec)
+    assert bits_equal(got, want), first_mismatch(got, want)
+
+
+def test_fp64_reference_gemm_vs_oracle():
+    g = torch.Generator().manual_seed(5)
+    a = as_operand(torch.randn(32, 1024, generator=g).bfloat16().cuda())
+    b = as_operand((torch.randn(40, 1024, generator=g) * 0.02).bfloat16().cuda())
+    spec = MMASpec("fp64", out_format="fp32")
+    got = gemm_triton(a, b, spec).cpu().numpy()
+    assert bits_equal(got, _oracle_gemm(a, b, spec))
+
+
+def test_errors():
+    a = Operand(torch.ones(2, 4, device="cuda"), IntFormat("int8", 8))
+    b = Operand(torch.tensor([[float("nan"), 1, 1, 1]], device="cuda"), IntFormat("int8", 8))
+    with pytest.raises(ValueError, match="finite"):
+        gemm_triton(a, b, MMASpec("int_exact"))
+    c = Operand(torch.ones(2, 5, device="cuda"), IntFormat("int8", 8))
+    with pytest.raises(ValueError, match="same K"):
+        gemm_triton(a, c, MMASpec("int_exact"))
+    wide = MMASpec("cofda", f_bits=48, chunk_size=2 ** 14)
+    with pytest.raises(ValueError, match="headroom"):
+        gemm_triton(a, Operand(torch.ones(3, 4, device="cuda"), IntFormat("int8", 8)), wide)

@@ -1,0 +1,46 @@
+// Descriptors shared by the GEMM kernels.
+#pragma once
+
+#include "tc_mma_exact.cuh"
+
+namespace tc {
+
+enum { ALG_COFDA = 0, ALG_GDFS = 1, ALG_FP32_FMA = 2, ALG_FP64 = 3, ALG_INT_EXACT = 4 };
+enum { AP_EPILOGUE = 0, AP_PRODUCT = 1, AP_GROUP = 2, AP_PROMOTE = 3, AP_OPERAND = 4 };
+enum { SK_NONE = 0, SK_TENSOR = 1, SK_ROW = 2, SK_K = 3 };
+
+struct OpDesc {
+  const void *v;
+  int dt;
+  int64_t rows, K;
+  Fmt f;
+  int radix;
+  const float *scale;
+  int skind;
+  Fmt sf;
+  int srad;
+  int kd;
+  int64_t nkd;
+  int field0;  // standard E8M0 K scale: 2**-127 counts as zero
+  const float *alpha;
+};
+
+struct GemmDesc {
+  OpDesc a, b;
+  int64_t M, N, K;
+  int alg, F, CS, decoupled, F2, G, GS, KT, rne, apply, PI;
+  Fmt of;
+  int out_dt;
+  int out_is_plain;  // out_format is fp32 itself: no output cast
+  const float *bias;
+  void *out;
+};
+
+int build_desc(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec, const float *bias, void *out,
+               GemmDesc &g);
+
+// Fast kernels (tc_gemm_fast.cu): return TC_UNSUPPORTED when the case is not theirs.
+size_t fast_workspace(const GemmDesc &g);
+int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
+
+}  // namespace tc

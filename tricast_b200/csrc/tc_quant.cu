@@ -1,0 +1,752 @@
+// Cast and quantize kernels (TriCast round_to_format / quantize, src/tricast/reference/cast.py and
+// src/tricast/reference/quantize.py).
+//
+// Quantize runs one of two pipelines:
+//  * fused group pass — granularity "group" with group_size in {4,...,128} dividing K: each group is
+//    owned by group_size/4 adjacent lanes that load 4 elements each with one vector load, reduce the
+//    domain statistic with warp shuffles, compute the scale, and write values / scale / codes /
+//    dequant in the same pass, so x is read from HBM once;
+//  * general pass — any granularity: (A) per-domain partial statistics, (B) one warp per domain
+//    combines partials and derives scale and zero point, (C) element rounding.
+// Two-level specs first reduce the tensor amax and derive the global decode scale d2 on the device.
+#include <cmath>
+#include <cstring>
+#include <string>
+
+#include "tc_common.cuh"
+
+namespace tc {
+
+enum { GRAN_TENSOR = 0, GRAN_ROW = 1, GRAN_GROUP = 2, GRAN_BLOCK = 3 };
+enum { M_ABSMAX = 0, M_POW2_FLOOR = 1, M_POW2_CEIL = 2, M_MSE = 3, M_PERCENTILE = 4 };
+enum { ZP_NONE = 0, ZP_INT = 1, ZP_FLOAT = 2 };
+
+struct QParams {
+  Fmt ef, sf;
+  int64_t rows, K;
+  int64_t dr, dc, nr, nc;  // nominal domain rect and domain grid
+  int has_scale, method, srnd, two_level, zp, rnd, sr_bits, saturate;
+  float max_elem;          // element max_normal (exact in fp32)
+  double max_elem_d;
+  int emax_elem;
+  uint32_t min_scale_bits;  // scale format min_subnormal (pow2: min_normal) as fp32
+  double qmin_d, qmax_d;
+  float qrange;             // qmax - qmin
+  int x_dtype, v_dtype;
+  int code_bits;            // 0, 4 or 8
+  int scode;                // 0 none, 1 byte code of the scale format
+  float prod_max;           // element max * scale max (two-level), only its double below is used
+  double prod_max_d;
+};
+
+// ------------------------------------------------------------------ element codes
+// Bit encoding of a grid value in a <= 8-bit format (sign | exponent field | fraction field, or
+// two's complement k for integers). NaN uses the format's NaN encoding where it has one.
+__device__ __forceinline__ uint32_t element_code(float v, const Fmt &f, int total_bits) {
+  uint32_t u = f2u(v);
+  uint32_t sign = u >> 31;
+  uint32_t a = u & 0x7FFFFFFFu;
+  if (f.kind == 1) {
+    if (a > kInf) return 0u;
+    double k = ldexp((double)fabsf(v), f.frac_bits);
+    int64_t ki = (int64_t)k;
+    if (sign && a) ki = -ki;
+    return (uint32_t)ki & ((1u << total_bits) - 1u);
+  }
+  int mb = f.mbits;
+  uint32_t mmask = (1u << mb) - 1u;
+  uint32_t top_field = (1u << f.ebits) - 1u;
+  uint32_t code;
+  if (a > kInf) {
+    if (f.special == 1) code = (top_field << mb) | mmask;                // fn: all ones
+    else if (f.special == 2) return 1u << (total_bits - 1);              // fnuz: the "-0" pattern
+    else if (f.special == 0) code = (top_field << mb) | (mb ? (1u << (mb - 1)) : 0u);
+    else code = 0u;
+    sign = 0;
+  } else if (a == kInf) {
+    code = top_field << mb;
+  } else if (a == 0) {
+    code = 0u;
+  } else {
+    int field = (int)(a >> 23);
+    int e32 = field ? field - 127 : -126;
+    uint32_t sig = field ? ((a & 0x7FFFFFu) | 0x800000u) : a;
+    if (e32 >= f.emin) {
+      code = ((uint32_t)(e32 + f.bias) << mb) | ((sig >> (23 - mb)) & mmask);
+    } else {
+      int s = 23 - mb + (f.emin - e32);   // fraction of a subnormal in units of 2**(emin - mbits)
+      code = s >= 32 ? 0u : (sig >> s);
+    }
+  }
+  if (f.is_signed) code |= sign << (f.ebits + mb);
+  return code & ((1u << total_bits) - 1u);
+}
+
+__device__ __forceinline__ uint32_t scale_code(float s, const Fmt &f) {
+  if (f.kind == 2) {
+    uint32_t a = f2u(s);
+    if ((a & 0x7FFFFFFFu) > kInf) return 0xFFu;
+    int e;
+    frexpf(s, &e);
+    return (uint32_t)(e - 1 + f.bias) & 0xFFu;
+  }
+  return element_code(s, f, f.ebits + f.mbits + (f.is_signed ? 1 : 0));
+}
+
+// ------------------------------------------------------------------ scale selection
+__device__ __forceinline__ float amax_scale(float amax, float d2, bool has_d2, const QParams &p, uint32_t noise) {
+  float t = __fdiv_rn(amax, p.max_elem);
+  if (has_d2) t = __fdiv_rn(t, d2);
+  float s = cast_to(t, p.sf, p.srnd, true, noise, 32);
+  if (s == 0.0f) s = u2f(p.min_scale_bits);
+  if (amax == 0.0f) s = 1.0f;
+  return s;
+}
+
+__device__ __forceinline__ float pow2_scale(float amax, const QParams &p) {
+  double a = amax == 0.0f ? ldexp(1.0, -126) : (double)amax;
+  int ex;
+  frexp(a, &ex);
+  int e = ex - 1 - p.emax_elem;
+  if (p.method == M_POW2_CEIL && ldexp(p.max_elem_d, e) < a) e += 1;
+  bool overflow = e > p.sf.emax || !isfinite(a);
+  e = e < p.sf.emin ? p.sf.emin : (e > p.sf.emax ? p.sf.emax : e);
+  float s = __double2float_rn(ldexp(1.0, e));
+  return overflow ? u2f(kQNaN) : s;
+}
+
+// One exact binary32 rounding of amax / P, P = element max * scale max, as TriCast's
+// _global_scale (src/tricast/reference/quantize.py:195-219): the fp64 quotient gives a candidate
+// and the midpoints to its neighbours are tested exactly with fma (the sign of m*P - amax).
+__device__ float global_scale(float amax, double P) {
+  if (!isfinite(amax)) return amax;
+  if (amax == 0.0f) return 1.0f;
+  double A = (double)amax;
+  float r = __double2float_rn(A / P);
+  for (int it = 0; it < 2; ++it) {
+    float up = nextafterf(r, INFINITY);
+    double mid = 0.5 * ((double)r + (double)up);
+    double s = fma(mid, P, -A);
+    if (s < 0 || (s == 0 && (f2u(r) & 1u))) r = up;
+    float dn = nextafterf(r, -INFINITY);
+    mid = 0.5 * ((double)r + (double)dn);
+    s = fma(mid, P, -A);
+    if (s > 0 || (s == 0 && (f2u(r) & 1u))) r = dn;
+  }
+  return r == 0.0f ? 1.0f : r;
+}
+
+// Affine scale and zero point from the domain range (src/tricast/reference/quantize.py:176-192).
+__device__ __forceinline__ void zp_scale(float lo, float hi, const QParams &p, uint32_t noise, float &s, float &z) {
+  if (p.zp == ZP_INT) {
+    if (lo > 0.0f) lo = 0.0f;  // clamp(max=0): keeps -0 and NaN
+    if (hi < 0.0f) hi = 0.0f;
+  }
+  float raw = __fdiv_rn(__fsub_rn(hi, lo), p.qrange);
+  s = cast_to(raw, p.sf, p.srnd, true, noise, 32);
+  if (s == 0.0f) s = u2f(p.min_scale_bits);
+  if (hi == lo) s = 1.0f;
+  z = lo;
+  if (p.zp == ZP_INT) {
+    float t = rintf(__fsub_rn((float)p.qmin_d, __fdiv_rn(lo, s)));
+    if (t < (float)p.qmin_d) t = (float)p.qmin_d;
+    if (t > (float)p.qmax_d) t = (float)p.qmax_d;
+    z = t;  // NaN stays NaN (both comparisons false)
+  }
+}
+
+// Order-preserving keys: -0 sorts below +0.
+__device__ __forceinline__ uint32_t fkey(float v) {
+  uint32_t u = f2u(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float unkey(uint32_t k) { return u2f((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k); }
+
+// ------------------------------------------------------------------ element rounding
+// Integer rounding for zero-point specs on the unbounded integer grid, then + z and clamp
+// (src/tricast/reference/quantize.py:325-332).
+__device__ __forceinline__ float zp_round(float xq, float z, const QParams &p, uint32_t noise) {
+  uint32_t u = f2u(xq);
+  uint32_t a = u & 0x7FFFFFFFu;
+  double r;
+  if (a > kInf) {
+    r = (double)xq;
+  } else if (a == kInf) {
+    r = (double)xq;
+  } else {
+    bool neg = (u >> 31) && a;
+    uint32_t field = a >> 23;
+    uint32_t sig = field ? ((a & 0x7FFFFFu) | 0x800000u) : a;
+    int e32 = field ? (int)field - 127 : -126;
+    int shift = 23 - e32;  // quantum 2**0
+    double k;
+    if (shift <= 0) {
+      k = (double)fabsf(xq);
+    } else {
+      uint32_t kept = shift >= 32 ? 0u : (sig >> shift);
+      uint32_t rem = shift >= 32 ? sig : (sig & ((1u << shift) - 1u));
+      kept += round_inc(kept, rem, shift, neg, p.rnd, noise, p.sr_bits) ? 1u : 0u;
+      k = (double)kept;
+    }
+    r = (u >> 31) ? -k : k;
+  }
+  if (p.zp == ZP_INT) r = r + (double)z;
+  if (r < p.qmin_d) r = p.qmin_d;
+  if (r > p.qmax_d) r = p.qmax_d;
+  return (float)r;
+}
+
+struct ElemOut {
+  float value;
+  float dequant;
+};
+
+__device__ __forceinline__ ElemOut quant_elem(float x, float s, float z, float d2, bool has_d2, const QParams &p,
+                                              uint32_t noise) {
+  float xq = x;
+  if (p.zp == ZP_FLOAT) xq = __fsub_rn(xq, z);
+  if (p.has_scale) {
+    float eff = has_d2 ? __fmul_rn(s, d2) : s;
+    xq = __fdiv_rn(xq, eff);
+  }
+  ElemOut o;
+  o.value = p.zp ? zp_round(xq, z, p, noise) : cast_to(xq, p.ef, p.rnd, p.saturate, noise, p.sr_bits);
+  float d = o.value;
+  if (p.zp == ZP_INT) d = __fsub_rn(d, z);
+  if (p.has_scale) d = __fmul_rn(d, s);
+  if (p.zp == ZP_FLOAT) d = __fadd_rn(d, z);
+  if (has_d2) d = __fmul_rn(d, d2);
+  o.dequant = d;
+  return o;
+}
+
+// ------------------------------------------------------------------ cast kernel
+__global__ void __launch_bounds__(256) cast_kernel(const float *__restrict__ x, float *__restrict__ y,
+                                                   const uint32_t *__restrict__ noise, int64_t n, Fmt f, int rnd,
+                                                   int saturate, int sr_bits, int vec) {
+  int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (vec) {
+    int64_t n4 = n >> 2;
+    for (int64_t i = tid; i < n4; i += stride) {
+      float4 v = reinterpret_cast<const float4 *>(x)[i];
+      uint4 r = noise ? reinterpret_cast<const uint4 *>(noise)[i] : make_uint4(0, 0, 0, 0);
+      float4 o;
+      o.x = cast_to(v.x, f, rnd, saturate, r.x, sr_bits);
+      o.y = cast_to(v.y, f, rnd, saturate, r.y, sr_bits);
+      o.z = cast_to(v.z, f, rnd, saturate, r.z, sr_bits);
+      o.w = cast_to(v.w, f, rnd, saturate, r.w, sr_bits);
+      reinterpret_cast<float4 *>(y)[i] = o;
+    }
+    for (int64_t i = (n4 << 2) + tid; i < n; i += stride)
+      y[i] = cast_to(x[i], f, rnd, saturate, noise ? noise[i] : 0u, sr_bits);
+  } else {
+    for (int64_t i = tid; i < n; i += stride) y[i] = cast_to(x[i], f, rnd, saturate, noise ? noise[i] : 0u, sr_bits);
+  }
+}
+
+static int sm_count() {
+  static int count = 0;
+  if (!count) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
+    if (count <= 0) count = 148;
+  }
+  return count;
+}
+
+static int grid_for(int64_t work, int threads, int per_sm = 8) {
+  int64_t blocks = (work + threads - 1) / threads;
+  int64_t cap = (int64_t)sm_count() * per_sm;
+  if (blocks > cap) blocks = cap;
+  return (int)(blocks < 1 ? 1 : blocks);
+}
+
+static int launch_status(const char *what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string(what) + ": " + cudaGetErrorString(e));
+    return TC_CUDA_ERROR;
+  }
+  return TC_OK;
+}
+
+// ------------------------------------------------------------------ general pass (A): statistics
+// Partial statistic of one (domain, part): amax bits (NaN-propagating max of |x| bits) or
+// (min key, max key, nan flag).
+struct Stat {
+  uint32_t amax, lo, hi, nan;
+};
+
+__device__ __forceinline__ void stat_init(Stat &s) {
+  s.amax = 0;
+  s.lo = 0xFFFFFFFFu;
+  s.hi = 0;
+  s.nan = 0;
+}
+__device__ __forceinline__ void stat_add(Stat &s, float v) {
+  uint32_t a = f2u(v) & 0x7FFFFFFFu;
+  s.amax = max(s.amax, a);
+  if (a > kInf) {
+    s.nan = 1;
+  } else {
+    uint32_t k = fkey(v);
+    s.lo = min(s.lo, k);
+    s.hi = max(s.hi, k);
+  }
+}
+__device__ __forceinline__ void stat_merge(Stat &s, const Stat &o) {
+  s.amax = max(s.amax, o.amax);
+  s.lo = min(s.lo, o.lo);
+  s.hi = max(s.hi, o.hi);
+  s.nan |= o.nan;
+}
+__device__ __forceinline__ Stat stat_shfl(const Stat &s, int lane_mask) {
+  Stat o;
+  o.amax = __shfl_xor_sync(0xFFFFFFFFu, s.amax, lane_mask);
+  o.lo = __shfl_xor_sync(0xFFFFFFFFu, s.lo, lane_mask);
+  o.hi = __shfl_xor_sync(0xFFFFFFFFu, s.hi, lane_mask);
+  o.nan = __shfl_xor_sync(0xFFFFFFFFu, s.nan, lane_mask);
+  return o;
+}
+
+// Domain d as a rectangle of x; element e of it in row-major order.
+__device__ __forceinline__ void domain_rect(const QParams &p, int64_t d, int64_t &r0, int64_t &c0, int64_t &h,
+                                            int64_t &w) {
+  int64_t dri = d / p.nc, dci = d % p.nc;
+  r0 = dri * p.dr;
+  c0 = dci * p.dc;
+  h = min(p.dr, p.rows - r0);
+  w = min(p.dc, p.K - c0);
+}
+
+__global__ void __launch_bounds__(256) stats_kernel(const void *__restrict__ x, QParams p, int64_t nd, int parts,
+                                                    int64_t chunk, Stat *__restrict__ partial) {
+  int64_t d = blockIdx.x / parts;
+  int part = blockIdx.x % parts;
+  if (d >= nd) return;
+  int64_t r0, c0, h, w;
+  domain_rect(p, d, r0, c0, h, w);
+  int64_t n = h * w;
+  int64_t beg = part * chunk, end = min(n, beg + chunk);
+  Stat s;
+  stat_init(s);
+  for (int64_t e = beg + threadIdx.x; e < end; e += blockDim.x) {
+    int64_t r = r0 + e / w, c = c0 + e % w;
+    stat_add(s, load_as_float(x, p.x_dtype, r * p.K + c));
+  }
+  for (int m = 16; m; m >>= 1) stat_merge(s, stat_shfl(s, m));
+  __shared__ Stat warp_stat[8];
+  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) warp_stat[warp] = s;
+  __syncthreads();
+  if (warp == 0) {
+    if (lane < (int)(blockDim.x >> 5)) s = warp_stat[lane];
+    else stat_init(s);
+    for (int m = 16; m; m >>= 1) stat_merge(s, stat_shfl(s, m));
+    if (lane == 0) partial[d * parts + part] = s;
+  }
+}
+
+// ------------------------------------------------------------------ general pass (B): scales
+// One warp per domain combines its partials and derives scale / zero point (and, for the
+// tensor-amax pre-pass of two-level specs, the global scale d2).
+__global__ void scale_kernel(QParams p, int64_t nd, int parts, const Stat *__restrict__ partial,
+                             const float *__restrict__ amax_override, float *__restrict__ d2_slot,
+                             const uint32_t *__restrict__ scale_noise, float *__restrict__ scale,
+                             float *__restrict__ zero, uint8_t *__restrict__ scodes, int global_only) {
+  int lane = threadIdx.x & 31;
+  int64_t d = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (d >= nd) return;
+  Stat s;
+  stat_init(s);
+  for (int i = lane; i < parts; i += 32) stat_merge(s, partial[d * parts + i]);
+  for (int m = 16; m; m >>= 1) stat_merge(s, stat_shfl(s, m));
+  if (lane) return;
+  float amax = amax_override ? *amax_override : u2f(s.amax);
+  if (global_only) {
+    *d2_slot = global_scale(amax, p.prod_max_d);
+    return;
+  }
+  uint32_t noise = scale_noise ? scale_noise[d] : 0u;
+  float sc, z = 0.0f;
+  if (p.zp) {
+    float lo = s.nan ? u2f(kQNaN) : unkey(s.lo);
+    float hi = s.nan ? u2f(kQNaN) : unkey(s.hi);
+    zp_scale(lo, hi, p, noise, sc, z);
+    zero[d] = z;
+  } else if (p.two_level || p.method == M_ABSMAX) {
+    sc = amax_scale(amax, p.two_level ? *d2_slot : 1.0f, p.two_level, p, noise);
+  } else {
+    sc = pow2_scale(amax, p);
+  }
+  scale[d] = sc;
+  if (scodes) scodes[d] = (uint8_t)scale_code(sc, p.sf);
+}
+
+// ------------------------------------------------------------------ general pass (C): elements
+__device__ __forceinline__ void store_codes(uint8_t *codes, int bits, int64_t i, uint32_t c, uint32_t c_next,
+                                            bool pair) {
+  if (bits == 8) {
+    codes[i] = (uint8_t)c;
+  } else if (pair) {
+    codes[i >> 1] = (uint8_t)((c & 0xF) | ((c_next & 0xF) << 4));
+  }
+}
+
+__global__ void __launch_bounds__(256) element_kernel(const void *__restrict__ x, QParams p,
+                                                      const float *__restrict__ scale, const float *__restrict__ zero,
+                                                      const float *__restrict__ d2p, const uint32_t *__restrict__ noise,
+                                                      void *__restrict__ values, uint8_t *__restrict__ codes,
+                                                      float *__restrict__ dequant) {
+  int64_t n = p.rows * p.K;
+  int64_t npairs = (n + 1) >> 1;
+  float d2 = p.two_level ? *d2p : 1.0f;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t pi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; pi < npairs; pi += stride) {
+    uint32_t cc[2] = {0, 0};
+    for (int j = 0; j < 2; ++j) {
+      int64_t i = 2 * pi + j;
+      if (i >= n) break;
+      int64_t r = i / p.K, c = i % p.K;
+      float s = 1.0f, z = 0.0f;
+      if (p.has_scale) {
+        int64_t d = (r / p.dr) * p.nc + c / p.dc;
+        s = scale[d];
+        if (p.zp) z = zero[d];
+      }
+      ElemOut o = quant_elem(load_as_float(x, p.x_dtype, i), s, z, d2, p.two_level, p, noise ? noise[i] : 0u);
+      store_container(values, p.v_dtype, i, o.value);
+      if (dequant) dequant[i] = o.dequant;
+      if (codes) cc[j] = element_code(o.value, p.ef, p.code_bits == 4 ? 4 : 8);
+    }
+    if (codes) {
+      if (p.code_bits == 8) {
+        codes[2 * pi] = (uint8_t)cc[0];
+        if (2 * pi + 1 < n) codes[2 * pi + 1] = (uint8_t)cc[1];
+      } else {
+        codes[pi] = (uint8_t)((cc[0] & 0xF) | ((cc[1] & 0xF) << 4));
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ fused group pass
+// L = group_size / 4 lanes own one group; each lane handles 4 consecutive elements.
+template <int L>
+__global__ void __launch_bounds__(256) group_kernel(const void *__restrict__ x, QParams p,
+                                                    const float *__restrict__ d2p, const uint32_t *__restrict__ noise,
+                                                    const uint32_t *__restrict__ scale_noise, void *__restrict__ values,
+                                                    float *__restrict__ scale, float *__restrict__ zero,
+                                                    uint8_t *__restrict__ codes, uint8_t *__restrict__ scodes,
+                                                    float *__restrict__ dequant) {
+  const int64_t n = p.rows * p.K;
+  const int64_t ngroups = n / (4 * L);
+  const float d2 = p.two_level ? *d2p : 1.0f;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % L;                    // position inside the group
+  constexpr int kGroupsPerWarp = 32 / L;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  // The trip count depends only on the warp, so every shuffle below sees the full warp.
+  for (int64_t base = warp * kGroupsPerWarp; base < ngroups; base += nwarps * kGroupsPerWarp) {
+    const int64_t g = base + lane / L;
+    const bool active = g < ngroups;
+    const int64_t i0 = g * (4 * L) + sub * 4;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (active) {
+      if (p.x_dtype == TC_F32) {
+        float4 t = *reinterpret_cast<const float4 *>(static_cast<const float *>(x) + i0);
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+      } else {
+        uint2 t = *reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(x) + i0);
+        uint16_t h[4] = {(uint16_t)(t.x & 0xFFFF), (uint16_t)(t.x >> 16), (uint16_t)(t.y & 0xFFFF),
+                         (uint16_t)(t.y >> 16)};
+        for (int j = 0; j < 4; ++j)
+          v[j] = p.x_dtype == TC_BF16 ? __bfloat162float(__ushort_as_bfloat16(h[j]))
+                                      : __half2float(__ushort_as_half(h[j]));
+      }
+    }
+    Stat s;
+    stat_init(s);
+    if (active)
+      for (int j = 0; j < 4; ++j) stat_add(s, v[j]);
+    for (int m = 1; m < L; m <<= 1) stat_merge(s, stat_shfl(s, m));
+    if (!active) continue;  // only in the last iteration; no shuffle follows
+    uint32_t sn = scale_noise ? scale_noise[g] : 0u;
+    float sc, z = 0.0f;
+    if (p.zp) {
+      float lo = s.nan ? u2f(kQNaN) : unkey(s.lo);
+      float hi = s.nan ? u2f(kQNaN) : unkey(s.hi);
+      zp_scale(lo, hi, p, sn, sc, z);
+    } else if (p.two_level || p.method == M_ABSMAX) {
+      sc = amax_scale(u2f(s.amax), d2, p.two_level, p, sn);
+    } else {
+      sc = pow2_scale(u2f(s.amax), p);
+    }
+    if (sub == 0) {
+      scale[g] = sc;
+      if (p.zp) zero[g] = z;
+      if (scodes) scodes[g] = (uint8_t)scale_code(sc, p.sf);
+    }
+    uint32_t nn[4] = {0u, 0u, 0u, 0u};
+    if (noise)
+      for (int j = 0; j < 4; ++j) nn[j] = noise[i0 + j];
+    float q[4], dq[4];
+    uint32_t cd[4];
+    for (int j = 0; j < 4; ++j) {
+      ElemOut o = quant_elem(v[j], sc, z, d2, p.two_level, p, nn[j]);
+      q[j] = o.value;
+      dq[j] = o.dequant;
+      cd[j] = codes ? element_code(o.value, p.ef, p.code_bits == 4 ? 4 : 8) : 0u;
+    }
+    if (p.v_dtype == TC_F32) {
+      *reinterpret_cast<float4 *>(static_cast<float *>(values) + i0) = make_float4(q[0], q[1], q[2], q[3]);
+    } else {
+      uint16_t h[4];
+      for (int j = 0; j < 4; ++j) {
+        uint32_t u = f2u(q[j]);
+        if (p.v_dtype == TC_BF16) h[j] = ((u & 0x7FFFFFFFu) > kInf) ? (uint16_t)0x7FC0 : (uint16_t)(u >> 16);
+        else h[j] = (q[j] != q[j]) ? (uint16_t)0x7E00 : __half_as_ushort(__float2half_rn(q[j]));
+      }
+      *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(values) + i0) =
+          make_uint2((uint32_t)h[0] | ((uint32_t)h[1] << 16), (uint32_t)h[2] | ((uint32_t)h[3] << 16));
+    }
+    if (dequant) *reinterpret_cast<float4 *>(dequant + i0) = make_float4(dq[0], dq[1], dq[2], dq[3]);
+    if (codes) {
+      if (p.code_bits == 4) {
+        *reinterpret_cast<uint16_t *>(codes + (i0 >> 1)) =
+            (uint16_t)((cd[0] & 0xF) | ((cd[1] & 0xF) << 4) | ((cd[2] & 0xF) << 8) | ((cd[3] & 0xF) << 12));
+      } else {
+        *reinterpret_cast<uint32_t *>(codes + i0) = (cd[0] & 0xFF) | ((cd[1] & 0xFF) << 8) |
+                                                    ((cd[2] & 0xFF) << 16) | ((cd[3] & 0xFF) << 24);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+static int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+static int stats_parts(int64_t domain_elems) {
+  int64_t parts = cdiv(domain_elems, 8192);
+  if (parts > 4096) parts = 4096;
+  return (int)(parts < 1 ? 1 : parts);
+}
+
+struct Plan {
+  QParams p;
+  int64_t nd;
+  int parts;          // per-domain partials of the general path
+  int tensor_parts;   // partials of the tensor-amax pre-pass
+  bool fused;
+  size_t ws_stats, ws_tensor, ws_d2, total;
+};
+
+static int make_plan(const void *x, int32_t x_dtype, int64_t rows, int64_t K, const tc_quant_spec *spec,
+                     const tc_quant_out *out, Plan &pl) {
+  std::memset(&pl, 0, sizeof(pl));
+  QParams &p = pl.p;
+  std::string err = fmt_error(spec->format);
+  if (!err.empty()) return set_error("element format: " + err), TC_INVALID_ARGUMENT;
+  if (spec->format.kind == 2) return set_error("e8m0 is a scale format, not an element format"), TC_INVALID_ARGUMENT;
+  if (rows <= 0 || K <= 0) return set_error("quantization needs a nonempty tensor of shape [..., K]"), TC_INVALID_ARGUMENT;
+  if (rows * K >= (1ll << 40)) return set_error("tensor too large"), TC_INVALID_ARGUMENT;
+  if (x_dtype < 0 || x_dtype > 2) return set_error("unsupported input dtype"), TC_INVALID_ARGUMENT;
+  if (spec->sr_bits < 1 || spec->sr_bits > 32) return set_error("sr_bits must be in [1, 32]"), TC_INVALID_ARGUMENT;
+  p.ef = derive(spec->format);
+  p.rows = rows;
+  p.K = K;
+  p.has_scale = spec->has_scale;
+  p.method = spec->scale_method;
+  p.srnd = spec->scale_rounding;
+  p.two_level = spec->has_scale && spec->two_level;
+  p.zp = spec->zero_point;
+  p.rnd = spec->rounding;
+  p.sr_bits = spec->sr_bits;
+  p.saturate = spec->saturate;
+  p.x_dtype = x_dtype;
+  p.v_dtype = out->values_dtype;
+  p.max_elem_d = fmt_max_normal(spec->format);
+  p.max_elem = (float)p.max_elem_d;
+  p.emax_elem = fmt_emax_elem(spec->format);
+  if (spec->format.kind == 1) {
+    p.qmin_d = (double)p.ef.qmin;
+    p.qmax_d = (double)p.ef.qmax;
+    p.qrange = (float)(p.ef.qmax - p.ef.qmin);
+  }
+  int total_bits = spec->format.kind == 0 ? spec->format.ebits + spec->format.mbits + (spec->format.is_signed ? 1 : 0)
+                                          : spec->format.bits;
+  if (out->codes) {
+    if (total_bits > 8) return set_error("element codes need a format of at most 8 bits"), TC_INVALID_ARGUMENT;
+    p.code_bits = total_bits <= 4 ? 4 : 8;
+    if (p.code_bits == 4 && ((rows * K) & 1)) return set_error("4-bit codes need an even element count"), TC_INVALID_ARGUMENT;
+  }
+  if (!spec->has_scale) {
+    if (spec->granularity != GRAN_TENSOR) return set_error("a direct cast (scale=None) has no granularity"), TC_INVALID_ARGUMENT;
+    if (spec->zero_point) return set_error("zero points need a scale"), TC_INVALID_ARGUMENT;
+    p.dr = rows; p.dc = K; p.nr = 1; p.nc = 1;
+    pl.nd = 0;
+    return TC_OK;
+  }
+  err = fmt_error(spec->scale_format);
+  if (!err.empty()) return set_error("scale format: " + err), TC_INVALID_ARGUMENT;
+  p.sf = derive(spec->scale_format);
+  p.min_scale_bits = p.sf.min_sub_bits;
+  if (spec->scale_format.kind == 0) {
+    uint32_t u;
+    float m = (float)fmt_min_scale(spec->scale_format);
+    std::memcpy(&u, &m, 4);
+    p.min_scale_bits = u;
+  }
+  p.prod_max_d = fmt_max_normal(spec->format) * fmt_max_normal(spec->scale_format);
+  if (out->scale_codes) {
+    int sbits = spec->scale_format.kind == 2 ? 8
+              : spec->scale_format.kind == 0 ? spec->scale_format.ebits + spec->scale_format.mbits + (spec->scale_format.is_signed ? 1 : 0)
+                                             : 99;
+    if (sbits > 8) return set_error("scale codes need a scale format of at most 8 bits"), TC_INVALID_ARGUMENT;
+    p.scode = 1;
+  }
+  if (spec->scale_method == M_MSE || spec->scale_method == M_PERCENTILE)
+    return set_error("mse / percentile scale selection is not implemented by this build"), TC_UNSUPPORTED;
+  switch (spec->granularity) {
+    case GRAN_TENSOR: p.dr = rows; p.dc = K; break;
+    case GRAN_ROW: p.dr = 1; p.dc = K; break;
+    case GRAN_GROUP:
+      if (spec->group_size <= 0) return set_error("granularity 'group' needs group_size > 0"), TC_INVALID_ARGUMENT;
+      p.dr = 1; p.dc = spec->group_size; break;
+    case GRAN_BLOCK:
+      if (spec->block_rows <= 0 || spec->block_cols <= 0)
+        return set_error("granularity 'block' needs block=(rows, cols) > 0"), TC_INVALID_ARGUMENT;
+      p.dr = spec->block_rows; p.dc = spec->block_cols; break;
+    default: return set_error("unknown granularity"), TC_INVALID_ARGUMENT;
+  }
+  if (p.dr > rows) p.dr = rows;
+  if (p.dc > K) p.dc = K;
+  p.nr = cdiv(rows, p.dr);
+  p.nc = cdiv(K, p.dc);
+  pl.nd = p.nr * p.nc;
+  int gs = (int)p.dc;
+  bool aligned = ((uintptr_t)x % (x_dtype == TC_F32 ? 16 : 8)) == 0;
+  pl.fused = spec->granularity == GRAN_GROUP && p.dr == 1 && K % gs == 0 && gs % 4 == 0 &&
+             (gs == 4 || gs == 8 || gs == 16 || gs == 32 || gs == 64 || gs == 128) && aligned &&
+             ((uintptr_t)out->values % 16) == 0 && (!out->dequant || ((uintptr_t)out->dequant % 16) == 0) &&
+             (!out->codes || ((uintptr_t)out->codes % 4) == 0);
+  pl.parts = stats_parts(p.dr * p.dc);
+  pl.tensor_parts = stats_parts(rows * K);
+  pl.ws_stats = pl.fused ? 0 : sizeof(Stat) * (size_t)pl.nd * pl.parts;
+  pl.ws_tensor = p.two_level ? sizeof(Stat) * (size_t)pl.tensor_parts : 0;
+  pl.ws_d2 = 0;
+  pl.total = ((pl.ws_stats + 255) & ~(size_t)255) + ((pl.ws_tensor + 255) & ~(size_t)255);
+  return TC_OK;
+}
+
+}  // namespace tc
+
+using namespace tc;
+
+extern "C" int tc_cast(const float *x, float *y, const uint32_t *noise, int64_t n, const tc_format *fmt,
+                       int32_t rounding, int32_t saturate, int32_t sr_bits, tc_stream stream) {
+  if (!fmt || (n > 0 && (!x || !y))) return set_error("tc_cast: null argument"), TC_INVALID_ARGUMENT;
+  std::string err = fmt_error(*fmt);
+  if (!err.empty()) return set_error("tc_cast: " + err), TC_INVALID_ARGUMENT;
+  if (rounding < 0 || rounding > 5) return set_error("tc_cast: unknown rounding"), TC_INVALID_ARGUMENT;
+  if (fmt->kind == 2 && rounding == TC_SR)
+    return set_error("stochastic rounding is not defined for power-of-two formats"), TC_INVALID_ARGUMENT;
+  if (sr_bits < 1 || sr_bits > 32) return set_error("sr_bits must be in [1, 32]"), TC_INVALID_ARGUMENT;
+  if (n <= 0) return TC_OK;
+  Fmt f = derive(*fmt);
+  int vec = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (!noise || (uintptr_t)noise % 16 == 0);
+  cast_kernel<<<grid_for(vec ? (n + 3) / 4 : n, 256), 256, 0, (cudaStream_t)stream>>>(x, y, noise, n, f, rounding,
+                                                                                   saturate, sr_bits, vec);
+  return launch_status("tc_cast");
+}
+
+extern "C" size_t tc_quantize_workspace(int64_t rows, int64_t K, const tc_quant_spec *spec) {
+  if (!spec) return 0;
+  Plan pl;
+  tc_quant_out dummy;
+  std::memset(&dummy, 0, sizeof(dummy));
+  // Alignment-independent upper bound: assume the general pass.
+  static float probe[4] __attribute__((aligned(16)));
+  if (make_plan(probe, TC_F32, rows, K, spec, &dummy, pl) != TC_OK) return 0;
+  size_t stats = sizeof(Stat) * (size_t)pl.nd * pl.parts;
+  return ((stats + 255) & ~(size_t)255) + ((pl.ws_tensor + 255) & ~(size_t)255);
+}
+
+extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t K, const tc_quant_spec *spec,
+                           const float *amax, const uint32_t *noise, const uint32_t *scale_noise,
+                           const tc_quant_out *out, void *workspace, size_t workspace_bytes, tc_stream stream) {
+  if (!x || !spec || !out || !out->values) return set_error("tc_quantize: null argument"), TC_INVALID_ARGUMENT;
+  Plan pl;
+  int st = make_plan(x, x_dtype, rows, K, spec, out, pl);
+  if (st) return st;
+  QParams &p = pl.p;
+  if (p.has_scale && (!out->scale || (p.zp && !out->zero_point) || (p.two_level && !out->global_scale)))
+    return set_error("tc_quantize: missing scale / zero_point / global_scale output"), TC_INVALID_ARGUMENT;
+  if (amax && spec->granularity != GRAN_TENSOR)
+    return set_error("amax override requires tensor granularity and a scalar"), TC_INVALID_ARGUMENT;
+  if (pl.total > workspace_bytes)
+    return set_error("tc_quantize: workspace too small"), TC_WORKSPACE_TOO_SMALL;
+  cudaStream_t s = (cudaStream_t)stream;
+  char *ws = static_cast<char *>(workspace);
+  Stat *stats = reinterpret_cast<Stat *>(ws);
+  Stat *tstats = reinterpret_cast<Stat *>(ws + ((pl.ws_stats + 255) & ~(size_t)255));
+  float *d2 = out->global_scale;
+  int64_t n = rows * K;
+  if (!p.has_scale) {
+    element_kernel<<<grid_for((n + 1) / 2, 256), 256, 0, s>>>(x, p, nullptr, nullptr, nullptr, noise, out->values,
+                                                             out->codes, out->dequant);
+    return launch_status("tc_quantize elements");
+  }
+  if (p.two_level) {
+    if (amax) {
+      // d2 from the override: one warp, no partials.
+      QParams q = p;
+      scale_kernel<<<1, 32, 0, s>>>(q, 1, 0, tstats, amax, d2, nullptr, nullptr, nullptr, nullptr, 1);
+    } else {
+      QParams q = p;
+      q.dr = rows; q.dc = K; q.nr = 1; q.nc = 1;
+      int64_t chunk = cdiv(n, pl.tensor_parts);
+      stats_kernel<<<pl.tensor_parts, 256, 0, s>>>(x, q, 1, pl.tensor_parts, chunk, tstats);
+      scale_kernel<<<1, 32, 0, s>>>(q, 1, pl.tensor_parts, tstats, nullptr, d2, nullptr, nullptr, nullptr, nullptr, 1);
+    }
+    if ((st = launch_status("tc_quantize global scale"))) return st;
+  }
+  if (pl.fused) {
+    int L = (int)(p.dc / 4);
+    int64_t ngroups = n / p.dc;
+    int64_t threads = ngroups * L;
+    int grid = grid_for(threads, 256, 16);
+#define TC_GROUP_CASE(LL)                                                                                     \
+  case LL:                                                                                                    \
+    group_kernel<LL><<<grid, 256, 0, s>>>(x, p, d2, noise, scale_noise, out->values, out->scale, out->zero_point, \
+                                          out->codes, out->scale_codes, out->dequant);                        \
+    break;
+    switch (L) {
+      TC_GROUP_CASE(1)
+      TC_GROUP_CASE(2)
+      TC_GROUP_CASE(4)
+      TC_GROUP_CASE(8)
+      TC_GROUP_CASE(16)
+      TC_GROUP_CASE(32)
+    }
+#undef TC_GROUP_CASE
+    return launch_status("tc_quantize group pass");
+  }
+  int64_t chunk = cdiv(p.dr * p.dc, pl.parts);
+  if (amax && !p.zp) {  // zero-point ranges always come from the data
+    scale_kernel<<<1, 32, 0, s>>>(p, 1, 0, stats, amax, d2, scale_noise, out->scale, out->zero_point,
+                                  out->scale_codes, 0);
+  } else {
+    stats_kernel<<<(unsigned)(pl.nd * pl.parts), 256, 0, s>>>(x, p, pl.nd, pl.parts, chunk, stats);
+    int64_t warps = pl.nd;
+    scale_kernel<<<(unsigned)cdiv(warps * 32, 256), 256, 0, s>>>(p, pl.nd, pl.parts, stats, nullptr, d2, scale_noise,
+                                                                out->scale, out->zero_point, out->scale_codes, 0);
+  }
+  if ((st = launch_status("tc_quantize scales"))) return st;
+  element_kernel<<<grid_for((n + 1) / 2, 256), 256, 0, s>>>(x, p, out->scale, out->zero_point, d2, noise, out->values,
+                                                           out->codes, out->dequant);
+  return launch_status("tc_quantize elements");
+}
