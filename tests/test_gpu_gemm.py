@@ -19,7 +19,7 @@ pytestmark = pytest.mark.gpu
 
 
 def _t(a):
-    return None if a is None else torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.float32))).cuda()
+    return None if a is None else torch.from_numpy(np.array(a, np.float32)).cuda()  # keeps 0-d shapes
 
 
 def cuda_operand(ns) -> Operand:
