@@ -1,0 +1,326 @@
+"""Benchmark of the TriCast emulation hot path on B200.
+
+Workload (the config the GEMM metric is quoted on): NVFP4 W4A4
+emulated GEMM. A = 2048x4096 bf16 ~ N(0,1) with 8 outlier channels x20, B = 4096x4096 bf16 ~
+N(0,0.02) (seeded, synthetic); one step = quantize A and B to NVFP4 (E2M1 elements, UE4M3 scale
+per 16 along K, fp32 tensor scale) + the Blackwell-FP4 GDFS emulated GEMM (G=6, F=35, GS=16,
+KT=64) with fp32 output, bit-exact with TriCast's reference backend.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Multi-GPU (torchrun, one rank per GPU): weak scaling by N-column slabs — every rank computes its
+own 4096-column slab of a (4096*N)-row weight against the same A; no collective on the data path.
+``--impl reference`` times the CPU oracle (numpy restatement of TriCast's reference backend) on
+the host cores over a bounded row slab of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "bit-exact emulated GEMM GMAC/s + cast GB/s per B200; 1/2/4/8-GPU layer-sweep secs"
+M, N, K = 2048, 4096, 4096
+WORKLOAD = ("cfg2 NVFP4 W4A4 emulated GEMM 2048x4096x4096: quantize A,B (nvfp4) + Blackwell-FP4 GDFS "
+            "(G=6,F=35,GS=16,KT=64) fp32 out")
+L2_FLUSH_BYTES = 512 << 20
+
+
+def make_inputs(rank: int):
+    """Seeded CPU generation so every GPU count sees identical tensors."""
+    import torch
+
+    g = torch.Generator().manual_seed(0)
+    a = torch.randn(M, K, generator=g)
+    a[:, torch.randperm(K, generator=g)[:8]] *= 20
+    gb = torch.Generator().manual_seed(1000 + rank)
+    b = torch.randn(N, K, generator=gb) * 0.02
+    return a.bfloat16(), b.bfloat16()
+
+
+def _smi_sampler(stop: threading.Event, samples: list, index: int) -> None:
+    q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    try:
+        proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200",
+                                 "-i", str(index)], stdout=subprocess.PIPE, text=True)
+    except OSError:
+        return
+    try:
+        while not stop.is_set():
+            line = proc.stdout.readline()
+            if not line:
+                break
+            samples.append([s.strip() for s in line.split(",")])
+    finally:
+        proc.terminate()
+        proc.wait(timeout=5)
+
+
+def clocks_summary(samples: list) -> dict:
+    if not samples:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+    sm = [float(s[1]) for s in samples if s[1].replace(".", "").isdigit()]
+    mx = [float(s[2]) for s in samples if s[2].replace(".", "").isdigit()]
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    reasons = sorted({names[i] for s in samples for i in range(4) if len(s) > 5 + i and s[5 + i].lower() == "active"})
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons, "samples": len(samples)}
+
+
+def measured_peaks() -> dict:
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "sm_max_mhz": 1965.0, "fallback": True}
+
+
+def cpu_oracle_sample(rows: int, cols: int, seed_rank: int = 0) -> tuple[float, str]:
+    """Oracle (numpy restatement of TriCast's reference backend) on a row x column slab with the
+    full K: quantize the slab of A and B, then the emulated GEMM. Returns (GMAC/s, description)."""
+    import numpy as np
+
+    import oracle
+    from oracle.quantize import quantize_reference
+    from tricast_b200.spec import PRESETS, SCHEMES
+
+    a, b = make_inputs(seed_rank)
+    a = a[:rows].float().numpy()
+    b = b[:cols].float().numpy()
+    spec = SCHEMES["nvfp4"]
+    t0 = time.perf_counter()
+    qa, qb = quantize_reference(a, spec), quantize_reference(b, spec)
+
+    class Op:
+        def __init__(self, q):
+            self.values, self.fmt, self.scale = q.values, spec.format, q.scale
+            self.scale_fmt, self.scale_kind, self.k_domain = spec.scale.format, "k", 16
+            self.alpha = np.float32(q.global_scale)
+
+    oracle.gemm_reference(Op(qa), Op(qb), PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32"))
+    dt = time.perf_counter() - t0
+    return rows * cols * K / dt / 1e9, f"{rows}x{cols}x{K} slab (quantize both + GDFS GEMM), {dt:.2f}s"
+
+
+_WORKER = {}
+
+
+def _init_worker(rows: int, cols: int) -> None:
+    """Pool initializer: the seeded inputs are generated once per worker process."""
+    a, b = make_inputs(0)
+    _WORKER["a"], _WORKER["b"] = a.float().numpy(), b[:cols].float().numpy()
+    _WORKER["rows"] = rows
+
+
+def _slab_worker(offset: int) -> int:
+    import numpy as np
+
+    import oracle
+    from oracle.quantize import quantize_reference
+    from tricast_b200.spec import PRESETS, SCHEMES
+
+    rows = _WORKER["rows"]
+    a = _WORKER["a"][offset:offset + rows]
+    b = _WORKER["b"]
+    spec = SCHEMES["nvfp4"]
+    qa, qb = quantize_reference(a, spec), quantize_reference(b, spec)
+
+    class Op:
+        def __init__(self, q):
+            self.values, self.fmt, self.scale = q.values, spec.format, q.scale
+            self.scale_fmt, self.scale_kind, self.k_domain = spec.scale.format, "k", 16
+            self.alpha = np.float32(q.global_scale)
+
+    oracle.gemm_reference(Op(qa), Op(qb), PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32"))
+    return rows * b.shape[0] * K
+
+
+def run_reference(args) -> None:
+    """CPU reference arm: the oracle port on all host cores, each step a bounded slab."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import multiprocessing as mp
+
+    cores = os.cpu_count() or 1
+    rows_per_worker, cols = 8, 1024
+    jobs = [i * rows_per_worker for i in range(cores)]
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(cores, initializer=_init_worker, initargs=(rows_per_worker, cols)) as pool:
+        for _ in range(args.warmup):
+            pool.map(_slab_worker, jobs[:1])
+        times = []
+        macs = 0
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            macs = sum(pool.map(_slab_worker, jobs))
+            times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = macs * args.steps / total / 1e9
+    sample = f"{cores} workers x ({rows_per_worker}x{cols}x{K} slab: quantize both + GDFS GEMM) per step"
+    line = {"metric": METRIC, "value": value, "unit": "GMAC/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64",
+            "data": "synthetic (seeded N(0,1)/N(0,0.02) bf16, 8 outlier channels x20)",
+            "config": {"workload": WORKLOAD, "global_batch": M, "sample": sample, "l2": "n/a (CPU)"},
+            "cpu_baseline": {"value": value, "unit": "GMAC/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "GMAC/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    from tricast_b200 import _native, as_operand, gemm_triton, quantize_triton
+    from tricast_b200.spec import PRESETS, SCHEMES
+
+    lib = _native.lib()
+    spec_q = SCHEMES["nvfp4"]
+    spec_m = PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32")
+    a_cpu, b_cpu = make_inputs(rank)
+    a, b = a_cpu.to(dev), b_cpu.to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    gemm_events = []
+
+    def step(xa, xb, record=False):
+        qa = quantize_triton(xa, spec_q)
+        qb = quantize_triton(xb, spec_q)
+        if record:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            out = gemm_triton(as_operand(qa), as_operand(qb), spec_m)
+            e1.record(stream)
+            gemm_events.append((e0, e1))
+        else:
+            out = gemm_triton(as_operand(qa), as_operand(qb), spec_m)
+        return out
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step(a, b)
+    barrier()
+
+    samples: list = []
+    stop = threading.Event()
+    sampler = threading.Thread(target=_smi_sampler, args=(stop, samples, local), daemon=True)
+    sampler.start()
+    time.sleep(0.3)
+    launches0 = lib.tc_launch_count()
+    barrier()
+    step_ms = []
+    for _ in range(args.steps):
+        flush.fill_(1)  # evict A/B/outputs from L2 between steps (outside the step's events)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        step(a, b, record=True)
+        s1.record(stream)
+        s1.synchronize()
+        step_ms.append(s0.elapsed_time(s1))
+    barrier()
+    launches = lib.tc_launch_count() - launches0
+
+    # End to end through the public API from pinned host memory: H2D of A and B, quantize + GEMM,
+    # D2H of the fp32 output, all inside the timed region.
+    ha, hb = a_cpu.pin_memory(), b_cpu.pin_memory()
+    hout = torch.empty((M, N), dtype=torch.float32).pin_memory()
+    e2e_ms = []
+    for i in range(args.warmup + args.steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        da, db = ha.to(dev, non_blocking=True), hb.to(dev, non_blocking=True)
+        out = step(da, db)
+        hout.copy_(out, non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+        if i >= args.warmup:
+            e2e_ms.append(e0.elapsed_time(e1))
+    barrier()
+    stop.set()
+    sampler.join(timeout=5)
+
+    t_step = sum(step_ms) / len(step_ms)
+    t_gemm = sum(e0.elapsed_time(e1) for e0, e1 in gemm_events) / len(gemm_events)
+    t_e2e = sum(e2e_ms) / len(e2e_ms)
+    stats = torch.tensor([t_step, t_gemm, t_e2e], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    t_step, t_gemm, t_e2e = stats.tolist()
+    macs = M * N * K
+    if rank == 0:
+        clk = clocks_summary(samples)
+        peaks = measured_peaks()
+        sm_mhz = clk["sm_mhz"] or peaks.get("sm_max_mhz", 1965.0)
+        ops_per_mac = 7.0
+        peak_gmacs = 148 * 128 * sm_mhz * 1e6 / ops_per_mac / 1e9
+        achieved = macs / (t_gemm * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": world * macs / (t_step * 1e-3) / 1e9, "unit": "GMAC/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int64",
+            "data": "synthetic (seeded N(0,1)/N(0,0.02) bf16, 8 outlier channels x20)",
+            "config": {"workload": WORKLOAD, "global_batch": M * world, "seq_len": K,
+                       "parallelism": f"n-slab x{world} (weak)", "l2": "flushed between steps (512 MiB write)"},
+            "e2e": {"value": world * macs / (t_e2e * 1e-3) / 1e9, "unit": "GMAC/s",
+                    "h2d_bytes_per_step": (M * K + N * K) * 2, "d2h_bytes_per_step": M * N * 4},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "alu", "achieved": achieved, "peak": peak_gmacs, "unit": "GMAC/s",
+                         "frac": achieved / peak_gmacs, "traffic": None,
+                         "note": f"emulated GEMM kernel; peak = 148 SMs x 128 lanes x {sm_mhz:.0f} MHz / "
+                                 f"{ops_per_mac:.0f} ops per MAC (two-pass GDFS)"},
+            "gemm_ms": t_gemm,
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            v, desc = cpu_oracle_sample(32, 512)
+            line["cpu_baseline"] = {"value": v, "unit": "GMAC/s", "cores": 1, "kind": "port", "sample": desc}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -173,6 +173,9 @@ int tc_error_stats(const void *ref, int32_t ref_dtype, const void *emu, int32_t 
 /* Message of the last failed call on this host thread ("" if none). */
 const char *tc_last_error(void);
 
+/* Number of kernels this library has launched in the process (all threads, all devices). */
+uint64_t tc_launch_count(void);
+
 /* Library version string. */
 const char *tc_version(void);
 

@@ -73,6 +73,7 @@ EXPORTS = {
     "tc_error_stats": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32, C.c_int64, C.c_void_p, C.c_void_p]),
     "tc_last_error": (C.c_char_p, []),
     "tc_version": (C.c_char_p, []),
+    "tc_launch_count": (C.c_uint64, []),
 }
 
 _lib = None

@@ -1,4 +1,5 @@
 // Host-side support of the C ABI: format derivation, thread-local error messages, version.
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -8,6 +9,9 @@
 namespace tc {
 
 static thread_local std::string g_last_error;
+static std::atomic<uint64_t> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 void set_error(const std::string &msg) { g_last_error = msg; }
 
@@ -119,5 +123,7 @@ Fmt derive(const tc_format &f) {
 }  // namespace tc
 
 extern "C" const char *tc_last_error(void) { return tc::g_last_error.c_str(); }
+
+extern "C" uint64_t tc_launch_count(void) { return tc::g_launches.load(std::memory_order_relaxed); }
 
 extern "C" const char *tc_version(void) { return "tricast_b200 0.1.0 (sm_100a)"; }

@@ -39,6 +39,7 @@ double fmt_max_normal(const tc_format &f);
 double fmt_min_scale(const tc_format &f);   // min_subnormal (floats) / min_normal (pow2)
 int fmt_emax_elem(const tc_format &f);      // floor(log2(max_normal))
 void set_error(const std::string &msg);
+void count_launch();  // every kernel launch of the library; read by tc_launch_count()
 
 // ---------------------------------------------------------------- small device helpers
 __host__ __device__ __forceinline__ uint32_t f2u(float v) {

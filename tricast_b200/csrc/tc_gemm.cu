@@ -351,6 +351,7 @@ extern "C" int tc_gemm(const tc_operand *a, const tc_operand *b, const tc_mma_sp
   dim3 grid((unsigned)((g.N + 15) / 16), (unsigned)((g.M + 15) / 16));
   if (grid.y > 65535) return set_error("tc_gemm: too many rows for the generic kernel"), TC_INVALID_ARGUMENT;
   gemm_generic_kernel<<<grid, 256, 0, s>>>(g);
+  ::tc::count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(std::string("tc_gemm: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
   return TC_OK;
@@ -362,6 +363,7 @@ extern "C" int tc_any_nonfinite(const void *values, int32_t dtype, int64_t n, in
   int64_t blocks = (n + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
   any_nonfinite_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(values, dtype, n, flag);
+  ::tc::count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(std::string("tc_any_nonfinite: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
   return TC_OK;

@@ -71,6 +71,7 @@ extern "C" int tc_error_stats(const void *ref, int32_t ref_dtype, const void *em
   int64_t blocks = (n + 255) / 256;
   if (blocks > 148 * 4) blocks = 148 * 4;
   tc::error_stats_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(ref, ref_dtype, emu, emu_dtype, n, sums);
+  ::tc::count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     tc::set_error(std::string("tc_error_stats: ") + cudaGetErrorString(e));

@@ -660,6 +660,7 @@ extern "C" int tc_cast(const float *x, float *y, const uint32_t *noise, int64_t 
   int vec = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (!noise || (uintptr_t)noise % 16 == 0);
   cast_kernel<<<grid_for(vec ? (n + 3) / 4 : n, 256), 256, 0, (cudaStream_t)stream>>>(x, y, noise, n, f, rounding,
                                                                                    saturate, sr_bits, vec);
+  ::tc::count_launch();
   return launch_status("tc_cast");
 }
 
@@ -698,6 +699,7 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
   if (!p.has_scale) {
     element_kernel<<<grid_for((n + 1) / 2, 256), 256, 0, s>>>(x, p, nullptr, nullptr, nullptr, noise, out->values,
                                                              out->codes, out->dequant);
+    ::tc::count_launch();
     return launch_status("tc_quantize elements");
   }
   if (p.two_level) {
@@ -705,12 +707,15 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
       // d2 from the override: one warp, no partials.
       QParams q = p;
       scale_kernel<<<1, 32, 0, s>>>(q, 1, 0, tstats, amax, d2, nullptr, nullptr, nullptr, nullptr, 1);
+      ::tc::count_launch();
     } else {
       QParams q = p;
       q.dr = rows; q.dc = K; q.nr = 1; q.nc = 1;
       int64_t chunk = cdiv(n, pl.tensor_parts);
       stats_kernel<<<pl.tensor_parts, 256, 0, s>>>(x, q, 1, pl.tensor_parts, chunk, tstats);
+      ::tc::count_launch();
       scale_kernel<<<1, 32, 0, s>>>(q, 1, pl.tensor_parts, tstats, nullptr, d2, nullptr, nullptr, nullptr, nullptr, 1);
+      ::tc::count_launch();
     }
     if ((st = launch_status("tc_quantize global scale"))) return st;
   }
@@ -723,6 +728,7 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
   case LL:                                                                                                    \
     group_kernel<LL><<<grid, 256, 0, s>>>(x, p, d2, noise, scale_noise, out->values, out->scale, out->zero_point, \
                                           out->codes, out->scale_codes, out->dequant);                        \
+    ::tc::count_launch();                                                                                     \
     break;
     switch (L) {
       TC_GROUP_CASE(1)
@@ -734,19 +740,24 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
     }
 #undef TC_GROUP_CASE
     return launch_status("tc_quantize group pass");
+    ::tc::count_launch();
   }
   int64_t chunk = cdiv(p.dr * p.dc, pl.parts);
   if (amax && !p.zp) {  // zero-point ranges always come from the data
     scale_kernel<<<1, 32, 0, s>>>(p, 1, 0, stats, amax, d2, scale_noise, out->scale, out->zero_point,
                                   out->scale_codes, 0);
+    ::tc::count_launch();
   } else {
     stats_kernel<<<(unsigned)(pl.nd * pl.parts), 256, 0, s>>>(x, p, pl.nd, pl.parts, chunk, stats);
+    ::tc::count_launch();
     int64_t warps = pl.nd;
     scale_kernel<<<(unsigned)cdiv(warps * 32, 256), 256, 0, s>>>(p, pl.nd, pl.parts, stats, nullptr, d2, scale_noise,
                                                                 out->scale, out->zero_point, out->scale_codes, 0);
+    ::tc::count_launch();
   }
   if ((st = launch_status("tc_quantize scales"))) return st;
   element_kernel<<<grid_for((n + 1) / 2, 256), 256, 0, s>>>(x, p, out->scale, out->zero_point, d2, noise, out->values,
                                                            out->codes, out->dequant);
+  ::tc::count_launch();
   return launch_status("tc_quantize elements");
 }
