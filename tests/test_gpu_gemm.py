@@ -119,3 +119,37 @@ def test_errors():
     wide = MMASpec("cofda", f_bits=48, chunk_size=2 ** 14)
     with pytest.raises(ValueError, match="headroom"):
         gemm_triton(a, Operand(torch.ones(3, 4, device="cuda"), IntFormat("int8", 8)), wide)
+
+
+@pytest.mark.parametrize("scheme", ["nvfp4", "mxfp4"])
+@pytest.mark.parametrize("shape", [(37, 70, 200), (1, 1, 16), (130, 65, 1040), (64, 64, 64)])
+def test_fp4_fast_path_ragged_shapes(scheme, shape):
+    """The fast GDFS kernel with partial CTA tiles, partial K tiles and partial groups."""
+    m, n, k = shape
+    a = _quantized(scheme, m, k, 11, outliers=min(3, k))
+    b = _quantized(scheme, n, k, 12, scale=0.02)
+    for preset in (PRESETS["nvidia_blackwell_fp4"], PRESETS["nvidia_blackwell_fp4"].with_(g_bits=9, f_bits=13),
+                   PRESETS["nvidia_blackwell_fp4"].with_(k_tile=128, norm_rounding="rne")):
+        spec = preset.with_(out_format="fp32")
+        got = gemm_triton(a, b, spec).cpu().numpy()
+        want = _oracle_gemm(a, b, spec)
+        assert bits_equal(got, want), f"{spec}: {first_mismatch(got, want)}"
+
+
+def test_fp4_fast_path_falls_back_on_specials():
+    """NaN operands and NaN / zero scales: the encoder flags them and the generic kernel runs."""
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(40, 256, generator=g)
+    x[3, 17] = float("nan")
+    a = as_operand(quantize_triton(x.cuda(), SCHEMES["nvfp4"]))
+    b = _quantized("nvfp4", 50, 256, 10, scale=0.02)
+    spec = PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32")
+    got = gemm_triton(a, b, spec).cpu().numpy()
+    assert bits_equal(got, _oracle_gemm(a, b, spec))
+    # A zero scale group (all-zero block) stays on the fast path and must act as a zero term.
+    x = torch.randn(40, 256, generator=g)
+    x[5, 32:48] = 0
+    a = as_operand(quantize_triton(x.cuda(), SCHEMES["mxfp4"]))
+    b = _quantized("mxfp4", 50, 256, 13)
+    got = gemm_triton(a, b, spec).cpu().numpy()
+    assert bits_equal(got, _oracle_gemm(a, b, spec))

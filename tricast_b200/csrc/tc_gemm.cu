@@ -158,7 +158,8 @@ __device__ __forceinline__ void store_out(const GemmDesc &g, int64_t m, int64_t 
   store_container(g.out, g.out_dt, m * g.N + n, v);
 }
 
-__global__ void __launch_bounds__(256) gemm_generic_kernel(GemmDesc g) {
+__global__ void __launch_bounds__(256) gemm_generic_kernel(GemmDesc g, const int32_t *only_if_flag) {
+  if (only_if_flag && *only_if_flag == 0) return;  // behind a fast kernel that took the product
   int64_t n = (int64_t)blockIdx.x * 16 + (threadIdx.x & 15);
   int64_t m = (int64_t)blockIdx.y * 16 + (threadIdx.x >> 4);
   if (m >= g.M || n >= g.N) return;
@@ -329,6 +330,12 @@ int build_desc(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec
   return TC_OK;
 }
 
+void launch_generic(const GemmDesc &g, const int32_t *only_if_flag, cudaStream_t s) {
+  dim3 grid((unsigned)((g.N + 15) / 16), (unsigned)((g.M + 15) / 16));
+  gemm_generic_kernel<<<grid, 256, 0, s>>>(g, only_if_flag);
+  count_launch();
+}
+
 }  // namespace tc
 
 using namespace tc;
@@ -348,10 +355,8 @@ extern "C" int tc_gemm(const tc_operand *a, const tc_operand *b, const tc_mma_sp
   cudaStream_t s = (cudaStream_t)stream;
   st = launch_fast(g, workspace, workspace_bytes, s);
   if (st != TC_UNSUPPORTED) return st;
-  dim3 grid((unsigned)((g.N + 15) / 16), (unsigned)((g.M + 15) / 16));
-  if (grid.y > 65535) return set_error("tc_gemm: too many rows for the generic kernel"), TC_INVALID_ARGUMENT;
-  gemm_generic_kernel<<<grid, 256, 0, s>>>(g);
-  ::tc::count_launch();
+  if ((g.M + 15) / 16 > 65535) return set_error("tc_gemm: too many rows for the generic kernel"), TC_INVALID_ARGUMENT;
+  launch_generic(g, nullptr, s);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(std::string("tc_gemm: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
   return TC_OK;

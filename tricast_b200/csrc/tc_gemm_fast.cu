@@ -1,10 +1,514 @@
-// Fast emulated-GEMM kernels (placeholder: every case goes to the exact generic kernel).
+// Fast emulated-GEMM kernels for the accumulation models the benchmark configurations use.
+//
+// GDFS with E2M1 x E2M1 operands and G >= 6 (the nvidia_blackwell_fp4 preset on NVFP4 / MXFP4
+// operands). Exactness argument (TriCast src/tricast/reference/mma.py:318-336): an E2M1 value is
+// m * 2**(e - 1) with m in {1, 2, 3} and e in {0, 1, 2}, so a product's decoded exponent is
+// ea + eb in [0, 4] and its significand m_a*m_b sits at radix 2. Moved to radix G and aligned to the
+// group maximum ge with a truncating right shift of ge - e <= 4 <= G - 2 bits, no product loses a
+// bit. The group sum is therefore S = 2**(G - 2 - ge) * D with D = sum (2a)(2b) the exact integer
+// dot product of the doubled codes (DP4A on int8 codes), and the group's aligned contribution to
+// the tile FDA at radix F is
+//     floor(|D| * ms_a * ms_b * 2**(F - 2 - srad + es_a + es_b - emax))
+// where (es, ms) are the decoded K-scale terms at radix srad and emax is the largest exponent
+// label ge + es_a + es_b over the tile's non-zero groups and the running value. ge itself only
+// enters through emax; it is the largest i + j such that some k has an A element of exponent
+// class >= i and a B element of class >= j, found with a few 16-bit mask ANDs per group.
+//
+// Operands are first encoded (encode_fp4_kernel) into 16-byte records per (K tile, group, row):
+// the sixteen int8 codes, the exponent-class masks, and the scale word. The GEMM kernel stages the
+// records of a 64-row x 64-column CTA tile through shared memory with 1-D TMA bulk copies
+// (cp.async.bulk, no multicast) completing on mbarriers, in a multi-stage ring. Every wait is
+// bounded; a timeout sets the device status word and the kernel returns.
+//
+// Any operand value or scale the fast path cannot take (NaN/Inf, off-grid values, wide scale
+// significands) raises a device flag during encoding; the fast kernel then writes nothing and the
+// exact generic kernel, launched behind it on the same stream, computes the product instead.
+#include <cstring>
+#include <string>
+
 #include "tc_gemm.cuh"
 
 namespace tc {
 
-size_t fast_workspace(const GemmDesc &) { return 0; }
+void launch_generic(const GemmDesc &g, const int32_t *only_if_flag, cudaStream_t s);
 
-int launch_fast(const GemmDesc &, void *, size_t, cudaStream_t) { return TC_UNSUPPORTED; }
+namespace fp4 {
+
+constexpr int kGS = 16;          // GDFS group size of the fast path
+constexpr int kTileRows = 64;    // rows (A) / columns (B) per CTA
+constexpr int kStages = 4;
+constexpr int kNone = -(1 << 28);  // "no active term" exponent
+
+// Scale word: es (int16, biased by 0x8000 in bits 0..15), ms (bits 16..23), sign (bit 24).
+__host__ __device__ __forceinline__ uint32_t pack_scale(int es, uint32_t ms, uint32_t neg) {
+  return ((uint32_t)(es + 0x8000) & 0xFFFFu) | ((ms & 0xFFu) << 16) | ((neg & 1u) << 24);
+}
+
+struct EncodeArgs {
+  const void *v;
+  int dt;
+  int64_t rows, K, rows_pad, ntiles;
+  int ng;                 // groups per K tile
+  const float *scale;     // K scales or nullptr
+  int64_t nkd;
+  int kd;
+  Fmt sf;
+  int field0;
+  uint4 *q;               // [ntiles * ng][rows_pad]
+  uint4 *m;
+  uint32_t *s;            // scale words [ntiles * ng][rows_pad]
+  int32_t *flag;          // set when the fast path cannot take this operand
+  int side;               // 0: A record layout, 1: B record layout
+};
+
+__global__ void __launch_bounds__(256) encode_fp4_kernel(EncodeArgs e) {
+  int64_t ngroups_row = e.ntiles * e.ng;
+  int64_t total = ngroups_row * e.rows_pad;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  bool bad = false;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+    int64_t gi = idx / e.rows_pad;       // group index along K
+    int64_t r = idx % e.rows_pad;        // consecutive threads take consecutive rows
+    int64_t k0 = gi * kGS;
+    uint32_t codes[4] = {0, 0, 0, 0};
+    uint32_t c0 = 0, c1 = 0, c2 = 0;     // exponent-class masks: >= 0 (nonzero), >= 1, >= 2
+    uint32_t sword = pack_scale(0, 0, 0);
+    if (r < e.rows) {
+      for (int j = 0; j < kGS; ++j) {
+        int64_t k = k0 + j;
+        int q = 0;
+        if (k < e.K) {
+          float v = load_as_float(e.v, e.dt, r * e.K + k);
+          float t = 2.0f * v;                 // exact for finite values
+          int ti = (int)t;
+          int at = ti < 0 ? -ti : ti;
+          bool on_grid = (float)ti == t && (at <= 4 || at == 6 || at == 8 || at == 12);
+          if (!on_grid) bad = true;           // also catches NaN / Inf
+          q = ti;
+          if (at) {
+            c0 |= 1u << j;
+            if (at >= 4) c1 |= 1u << j;       // |v| >= 2: exponent class 1 or 2
+            if (at >= 8) c2 |= 1u << j;       // |v| >= 4: exponent class 2
+          }
+        }
+        codes[j >> 2] |= ((uint32_t)(q & 0xFF)) << (8 * (j & 3));
+      }
+      int es = 0;
+      uint32_t ms = 1, neg = 0;
+      bool zero = false;
+      if (e.scale) {
+        float s = e.scale[r * e.nkd + k0 / e.kd];
+        Term t = decode_term(s, e.sf);
+        // Scale significands up to 4 bits (UE4M3, E4M3, E8M0) keep |D| * ms_a * ms_b < 2**20.
+        if (t.nan || t.inf || t.sig > 15 || t.exp < -30000 || t.exp > 30000) bad = true;
+        zero = t.zero || (e.field0 && f2u(s) == 0x00400000u);
+        es = t.exp;
+        ms = (uint32_t)t.sig;
+        neg = t.neg ? 1u : 0u;
+      }
+      if (zero) {
+        // A zero scale makes the whole group a zero term (the group rule of mma.py:270-276);
+        // zero codes give D = 0 for every partner, so the group never enters emax.
+        codes[0] = codes[1] = codes[2] = codes[3] = 0;
+        c0 = c1 = c2 = 0;
+        sword = pack_scale(0, 0, 0);
+      } else {
+        sword = pack_scale(es, ms, neg);
+      }
+    }
+    uint4 q4 = make_uint4(codes[0], codes[1], codes[2], codes[3]);
+    uint4 m4;
+    if (e.side == 0) {
+      m4 = make_uint4(c0 | (c1 << 16), c2 | (c1 << 16), c2, c2);
+    } else {
+      m4 = make_uint4(c1 | (c0 << 16), c1 | (c2 << 16), c0, c2 | (c1 << 16));
+    }
+    e.q[idx] = q4;
+    e.m[idx] = m4;
+    e.s[idx] = sword;
+  }
+  if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicExch(e.flag, 1);
+}
+
+struct GemmArgs {
+  const uint4 *aq, *am, *bq, *bm;
+  const uint32_t *as, *bs;
+  int64_t a_rows_pad, b_rows_pad;
+  int64_t M, N, ntiles;
+  int F, shift0;       // shift0 = F - 2 - srad (srad = radix of the combined scale)
+  int rne;
+  const float *alpha_a, *alpha_b, *bias;
+  Fmt of;
+  int out_plain, out_dt;
+  void *out;
+  const int32_t *flag;   // nonzero: the fast path is not valid for these operands
+  int32_t *status;       // set to 1 when a bounded wait gives up
+};
+
+// ---------------------------------------------------------------- mbarrier / bulk-copy helpers
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: gives up after ~2**22 polls (each try_wait itself suspends for a while).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  for (int i = 0; i < (1 << 22); ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+template <int NG>
+struct Stage {
+  uint4 aq[NG][kTileRows];
+  uint4 am[NG][kTileRows];
+  uint4 bq[NG][kTileRows];
+  uint4 bm[NG][kTileRows];
+  uint32_t as[NG][kTileRows];
+  uint32_t bs[NG][kTileRows];
+};
+
+__device__ __forceinline__ int exp_class_max(const uint4 &a, const uint4 &b) {
+  // a = {A0|A1<<16, A2|A1<<16, A2, A2}, b = {B1|B0<<16, B1|B2<<16, B0, B2|B1<<16}
+  uint32_t t1 = a.x & b.x;                  // A0&B1 | A1&B0        (sum >= 1)
+  uint32_t t2 = (a.x & b.w) | (a.z & b.z);  // A0&B2 | A1&B1 | A2&B0 (sum >= 2)
+  uint32_t t3 = a.y & b.y;                  // A2&B1 | A1&B2        (sum >= 3)
+  uint32_t t4 = a.w & b.w;                  // A2&B2                (sum = 4; a.w has no high half)
+  return (int)(t1 != 0) + (int)(t2 != 0) + (int)(t3 != 0) + (int)(t4 != 0);
+}
+
+__device__ __forceinline__ int dot16(const uint4 &a, const uint4 &b) {
+  int d = __dp4a((int)a.x, (int)b.x, 0);
+  d = __dp4a((int)a.y, (int)b.y, d);
+  d = __dp4a((int)a.z, (int)b.z, d);
+  return __dp4a((int)a.w, (int)b.w, d);
+}
+
+__device__ __forceinline__ int scale_exp(uint32_t w) { return (int)(w & 0xFFFFu) - 0x8000; }
+
+// Exponent of the running value as an FDA term (mma.py:85-91); kNone for 0 / Inf / NaN.
+__device__ __forceinline__ int running_exp(float c) {
+  uint32_t a = f2u(c) & 0x7FFFFFFFu;
+  if (a == 0 || a >= kInf) return kNone;
+  uint32_t field = a >> 23;
+  if (field) return (int)field - 127;
+  return ilog2_u32(a) - 149;
+}
+
+// The running value's significand at radix F, aligned to emax with truncation, signed.
+__device__ __forceinline__ int64_t running_term(float c, int F, int emax) {
+  uint32_t a = f2u(c) & 0x7FFFFFFFu;
+  if (a == 0 || a >= kInf) return 0;
+  uint32_t field = a >> 23;
+  uint32_t sig = field ? ((a & 0x7FFFFFu) | 0x800000u) : a;
+  int lead = ilog2_u32(sig);
+  int ec = (field ? (int)field - 127 : -126) + lead - 23;
+  uint64_t m = (uint64_t)(sig << (23 - lead));  // 24-bit, leading one at bit 23
+  int sh = (F - 23) - (emax - ec);
+  uint64_t v = sh >= 0 ? (m << sh) : (sh <= -64 ? 0ull : (m >> -sh));
+  return (f2u(c) >> 31) ? -(int64_t)v : (int64_t)v;
+}
+
+// 256 threads as 16 x 16; thread (ty, tx) owns rows ty*4 + i and columns tx + 16*j of the tile.
+template <int NG>
+__global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
+  if (*g.flag) return;  // the generic kernel takes over
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  Stage<NG> *stages = reinterpret_cast<Stage<NG> *>(smem_raw);
+  __shared__ __align__(8) uint64_t full[kStages];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t m0 = (int64_t)blockIdx.y * kTileRows, n0 = (int64_t)blockIdx.x * kTileRows;
+  constexpr uint32_t kRec = kTileRows * sizeof(uint4);
+  constexpr uint32_t kSw = kTileRows * sizeof(uint32_t);
+  constexpr uint32_t kStageBytes = NG * (4 * kRec + 2 * kSw);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int64_t t, int s) {
+    Stage<NG> &st = stages[s];
+    mbar_expect_tx(&full[s], kStageBytes);
+    for (int gg = 0; gg < NG; ++gg) {
+      int64_t ga = (t * NG + gg) * g.a_rows_pad + m0;
+      int64_t gb = (t * NG + gg) * g.b_rows_pad + n0;
+      bulk_g2s(st.aq[gg], g.aq + ga, kRec, &full[s]);
+      bulk_g2s(st.am[gg], g.am + ga, kRec, &full[s]);
+      bulk_g2s(st.as[gg], g.as + ga, kSw, &full[s]);
+      bulk_g2s(st.bq[gg], g.bq + gb, kRec, &full[s]);
+      bulk_g2s(st.bm[gg], g.bm + gb, kRec, &full[s]);
+      bulk_g2s(st.bs[gg], g.bs + gb, kSw, &full[s]);
+    }
+  };
+  if (threadIdx.x == 0)
+    for (int s = 0; s < kStages && s < g.ntiles; ++s) issue(s, s);
+
+  float c[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) c[i][j] = 0.0f;
+
+  bool timed_out = false;
+  for (int64_t t = 0; t < g.ntiles; ++t) {
+    const int s = (int)(t % kStages);
+    if (!mbar_wait(&full[s], (uint32_t)((t / kStages) & 1))) {
+      timed_out = true;
+    }
+    if (__syncthreads_or(timed_out)) {
+      if (threadIdx.x == 0) atomicExch(g.status, 1);
+      return;
+    }
+    const Stage<NG> &st = stages[s];
+    // Pass 1: exponent labels. emax starts at the running value's exponent (kNone if it is zero).
+    int emax[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) emax[i][j] = running_exp(c[i][j]);
+#pragma unroll 1
+    for (int gg = 0; gg < NG; ++gg) {
+      uint4 bq[4], bm[4];
+      int eb[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        bq[j] = st.bq[gg][tx + 16 * j];
+        bm[j] = st.bm[gg][tx + 16 * j];
+        eb[j] = scale_exp(st.bs[gg][tx + 16 * j]);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 aq = st.aq[gg][ty * 4 + i];
+        const uint4 am = st.am[gg][ty * 4 + i];
+        const int ea = scale_exp(st.as[gg][ty * 4 + i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          int d = dot16(aq, bq[j]);
+          int label = exp_class_max(am, bm[j]) + ea + eb[j];
+          if (d != 0 && label > emax[i][j]) emax[i][j] = label;
+        }
+      }
+    }
+    // Pass 2: exact aligned sum at radix F (int64), starting from the running value's term.
+    int64_t total[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) total[i][j] = running_term(c[i][j], g.F, emax[i][j]);
+#pragma unroll 1
+    for (int gg = 0; gg < NG; ++gg) {
+      uint4 bq[4];
+      uint32_t sb[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        bq[j] = st.bq[gg][tx + 16 * j];
+        sb[j] = st.bs[gg][tx + 16 * j];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 aq = st.aq[gg][ty * 4 + i];
+        const uint32_t sa = st.as[gg][ty * 4 + i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          int d = dot16(aq, bq[j]);
+          uint32_t x = (uint32_t)(d < 0 ? -d : d) * (((sa >> 16) & 0xFFu) * ((sb[j] >> 16) & 0xFFu));
+          int sh = g.shift0 + scale_exp(sa) + scale_exp(sb[j]) - emax[i][j];
+          // x < 2**20 and sh <= shift0 <= 40: (x << 40) >> (40 - sh) is the exact truncation.
+          int r = max(40 - sh, 0);  // sh > 40 only for d == 0 (x == 0)
+          uint64_t v = r >= 64 ? 0ull : (((uint64_t)x << 40) >> r);
+          bool neg = (d < 0) != (((sa ^ sb[j]) >> 24) & 1u);
+          total[i][j] += neg ? -(int64_t)v : (int64_t)v;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
+        if (cb >= kInf) continue;                 // Inf/NaN running value is sticky
+        if (emax[i][j] == kNone) continue;        // every term zero: keep c
+        c[i][j] = fixed_to_fp32(total[i][j], emax[i][j], g.F, g.rne, true);
+      }
+    __syncthreads();  // everyone is done with stage s
+    if (threadIdx.x == 0 && t + kStages < g.ntiles) issue(t + kStages, s);
+  }
+  // Epilogue: alpha, bias, output rounding (src/tricast/reference/mma.py:376-384).
+  float alpha = 1.0f;
+  bool has_alpha = g.alpha_a || g.alpha_b;
+  if (g.alpha_a) alpha = *g.alpha_a;
+  if (g.alpha_b) alpha = g.alpha_a ? __fmul_rn(alpha, *g.alpha_b) : *g.alpha_b;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int64_t m = m0 + ty * 4 + i, n = n0 + tx + 16 * j;
+      if (m >= g.M || n >= g.N) continue;
+      float acc = c[i][j];
+      if (has_alpha) acc = __fmul_rn(alpha, acc);
+      if (g.bias) acc = __fadd_rn(acc, g.bias[n]);
+      if (!g.out_plain) acc = cast_to(acc, g.of, TC_RNE, false, 0u, 32);
+      store_container(g.out, g.out_dt, m * g.N + n, acc);
+    }
+}
+
+}  // namespace fp4
+
+// ---------------------------------------------------------------- dispatch
+struct Fp4Plan {
+  bool ok;
+  int ng;
+  int64_t ntiles, a_pad, b_pad;
+  size_t off[6], bytes[6], flag_off, total;
+};
+
+static bool is_e2m1(const Fmt &f) { return f.kind == 0 && f.mbits == 1 && f.emin == 0 && f.emax == 2 && f.is_signed; }
+
+static Fp4Plan plan_fp4(const GemmDesc &g) {
+  Fp4Plan p;
+  std::memset(&p, 0, sizeof(p));
+  if (g.alg != ALG_GDFS || g.GS != fp4::kGS || g.G < 6 || g.KT % fp4::kGS) return p;
+  if (!is_e2m1(g.a.f) || !is_e2m1(g.b.f)) return p;
+  if (g.apply != AP_GROUP && (g.a.skind == SK_K || g.b.skind == SK_K)) return p;
+  if (g.a.skind == SK_TENSOR || g.a.skind == SK_ROW || g.b.skind == SK_TENSOR || g.b.skind == SK_ROW) return p;
+  if ((g.a.skind == SK_K && g.a.kd % fp4::kGS) || (g.b.skind == SK_K && g.b.kd % fp4::kGS)) return p;
+  int srad = (g.a.skind == SK_K ? g.a.srad : 0) + (g.b.skind == SK_K ? g.b.srad : 0);
+  int shift0 = g.F - 2 - srad;
+  if (shift0 > 40 || shift0 < -20) return p;
+  p.ng = g.KT / fp4::kGS;
+  if (p.ng != 1 && p.ng != 2 && p.ng != 4 && p.ng != 8) return p;
+  p.ntiles = (g.K + g.KT - 1) / g.KT;
+  p.a_pad = (g.M + fp4::kTileRows - 1) / fp4::kTileRows * fp4::kTileRows;
+  p.b_pad = (g.N + fp4::kTileRows - 1) / fp4::kTileRows * fp4::kTileRows;
+  int64_t ga = p.ntiles * p.ng * p.a_pad, gb = p.ntiles * p.ng * p.b_pad;
+  size_t sizes[6] = {(size_t)ga * 16, (size_t)ga * 16, (size_t)ga * 4, (size_t)gb * 16, (size_t)gb * 16, (size_t)gb * 4};
+  size_t off = 0;
+  for (int i = 0; i < 6; ++i) {
+    p.off[i] = off;
+    p.bytes[i] = sizes[i];
+    off += (sizes[i] + 255) & ~(size_t)255;
+  }
+  p.flag_off = off;
+  p.total = off + 256;
+  p.ok = true;
+  return p;
+}
+
+size_t fast_workspace(const GemmDesc &g) {
+  Fp4Plan p = plan_fp4(g);
+  return p.ok ? p.total : 0;
+}
+
+template <int NG>
+static int launch_fp4_gemm(const fp4::GemmArgs &args, int64_t M, int64_t N, cudaStream_t s) {
+  size_t smem = sizeof(fp4::Stage<NG>) * fp4::kStages;
+  cudaError_t e = cudaFuncSetAttribute(fp4::gdfs_fp4_kernel<NG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return set_error(std::string("gdfs fp4: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
+  dim3 grid((unsigned)((N + fp4::kTileRows - 1) / fp4::kTileRows), (unsigned)((M + fp4::kTileRows - 1) / fp4::kTileRows));
+  fp4::gdfs_fp4_kernel<NG><<<grid, 256, smem, s>>>(args);
+  count_launch();
+  return TC_OK;
+}
+
+int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s) {
+  Fp4Plan p = plan_fp4(g);
+  if (!p.ok) return TC_UNSUPPORTED;
+  if (!workspace || workspace_bytes < p.total) return set_error("tc_gemm: workspace too small"), TC_WORKSPACE_TOO_SMALL;
+  if (p.ntiles * fp4::kTileRows > (int64_t)1 << 40) return TC_UNSUPPORTED;
+  char *ws = static_cast<char *>(workspace);
+  int32_t *flag = reinterpret_cast<int32_t *>(ws + p.flag_off);
+  cudaMemsetAsync(flag, 0, 2 * sizeof(int32_t), s);
+  for (int side = 0; side < 2; ++side) {
+    const OpDesc &o = side ? g.b : g.a;
+    fp4::EncodeArgs e;
+    e.v = o.v;
+    e.dt = o.dt;
+    e.rows = o.rows;
+    e.K = o.K;
+    e.rows_pad = side ? p.b_pad : p.a_pad;
+    e.ntiles = p.ntiles;
+    e.ng = p.ng;
+    e.scale = o.skind == SK_K ? o.scale : nullptr;
+    e.nkd = o.nkd;
+    e.kd = o.kd;
+    e.sf = o.sf;
+    e.field0 = o.field0;
+    e.q = reinterpret_cast<uint4 *>(ws + p.off[side * 3 + 0]);
+    e.m = reinterpret_cast<uint4 *>(ws + p.off[side * 3 + 1]);
+    e.s = reinterpret_cast<uint32_t *>(ws + p.off[side * 3 + 2]);
+    e.flag = flag;
+    e.side = side;
+    int64_t work = p.ntiles * p.ng * e.rows_pad;
+    int64_t blocks = (work + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    fp4::encode_fp4_kernel<<<(unsigned)blocks, 256, 0, s>>>(e);
+    count_launch();
+  }
+  fp4::GemmArgs a;
+  a.aq = reinterpret_cast<const uint4 *>(ws + p.off[0]);
+  a.am = reinterpret_cast<const uint4 *>(ws + p.off[1]);
+  a.as = reinterpret_cast<const uint32_t *>(ws + p.off[2]);
+  a.bq = reinterpret_cast<const uint4 *>(ws + p.off[3]);
+  a.bm = reinterpret_cast<const uint4 *>(ws + p.off[4]);
+  a.bs = reinterpret_cast<const uint32_t *>(ws + p.off[5]);
+  a.a_rows_pad = p.a_pad;
+  a.b_rows_pad = p.b_pad;
+  a.M = g.M;
+  a.N = g.N;
+  a.ntiles = p.ntiles;
+  a.F = g.F;
+  int srad = (g.a.skind == SK_K ? g.a.srad : 0) + (g.b.skind == SK_K ? g.b.srad : 0);
+  a.shift0 = g.F - 2 - srad;
+  a.rne = g.rne;
+  a.alpha_a = g.a.alpha;
+  a.alpha_b = g.b.alpha;
+  a.bias = g.bias;
+  a.of = g.of;
+  a.out_plain = g.out_is_plain;
+  a.out_dt = g.out_dt;
+  a.out = g.out;
+  a.flag = flag;
+  a.status = flag + 1;
+  int st;
+  switch (p.ng) {
+    case 1: st = launch_fp4_gemm<1>(a, g.M, g.N, s); break;
+    case 2: st = launch_fp4_gemm<2>(a, g.M, g.N, s); break;
+    case 4: st = launch_fp4_gemm<4>(a, g.M, g.N, s); break;
+    default: st = launch_fp4_gemm<8>(a, g.M, g.N, s); break;
+  }
+  if (st) return st;
+  launch_generic(g, flag, s);  // runs only when the encoder raised the flag
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(std::string("tc_gemm fast: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
+  return TC_OK;
+}
 
 }  // namespace tc
