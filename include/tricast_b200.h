@@ -161,6 +161,17 @@ size_t tc_gemm_workspace(const tc_operand *a, const tc_operand *b, const tc_mma_
 int tc_gemm(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec, const float *bias, void *out,
             void *workspace, size_t workspace_bytes, tc_stream stream);
 
+/* tc_gemm for callers that cannot allocate device memory. No counterpart in TriCast: this entry point
+ * exists for hosts that reach the library through a bare C FFI without a CUDA allocator of their own,
+ * or that reserve all device memory up front, and so cannot hand tc_gemm a workspace. Same
+ * arguments and result as tc_gemm minus the workspace; the scratch comes from a fixed 32 MiB array
+ * inside the library (held on every GPU that loads the library, until exit). Operands whose
+ * tc_gemm_workspace() exceeds 32 MiB are rejected with TC_INVALID_ARGUMENT. The first call on a
+ * device looks up that array's device address, so make it before any stream capture. All calls
+ * share the array: calls whose GPU work can overlap race and must not be issued. Allocates nothing. */
+int tc_gemm_noalloc(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec, const float *bias,
+                    void *out, tc_stream stream);
+
 /* Device-side check used before int_exact: writes 1 to *flag (device int32) when any value of the
  * operand is NaN/Inf, else leaves it unchanged. */
 int tc_any_nonfinite(const void *values, int32_t dtype, int64_t n, int32_t *flag, tc_stream stream);

@@ -69,6 +69,8 @@ EXPORTS = {
     "tc_gemm_workspace": (C.c_size_t, [C.POINTER(TcOperand), C.POINTER(TcOperand), C.POINTER(TcMmaSpec)]),
     "tc_gemm": (C.c_int, [C.POINTER(TcOperand), C.POINTER(TcOperand), C.POINTER(TcMmaSpec), C.c_void_p, C.c_void_p,
                           C.c_void_p, C.c_size_t, C.c_void_p]),
+    "tc_gemm_noalloc": (C.c_int, [C.POINTER(TcOperand), C.POINTER(TcOperand), C.POINTER(TcMmaSpec), C.c_void_p,
+                                  C.c_void_p, C.c_void_p]),
     "tc_any_nonfinite": (C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_void_p, C.c_void_p]),
     "tc_error_stats": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32, C.c_int64, C.c_void_p, C.c_void_p]),
     "tc_last_error": (C.c_char_p, []),

@@ -43,4 +43,7 @@ int build_desc(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec
 size_t fast_workspace(const GemmDesc &g);
 int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
 
+// The exact generic kernel; with only_if_flag it runs only when *only_if_flag != 0.
+void launch_generic(const GemmDesc &g, const int32_t *only_if_flag, cudaStream_t s);
+
 }  // namespace tc

@@ -30,8 +30,6 @@
 
 namespace tc {
 
-void launch_generic(const GemmDesc &g, const int32_t *only_if_flag, cudaStream_t s);
-
 namespace fp4 {
 
 constexpr int kGS = 16;          // GDFS group size of the fast path
