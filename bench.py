@@ -36,6 +36,55 @@ WORKLOAD = ("cfg2 NVFP4 W4A4 emulated GEMM 2048x4096x4096: quantize A,B (nvfp4) 
 L2_FLUSH_BYTES = 512 << 20
 
 
+CFG1_BYTES_PER_ELEM = 4 + 4 + 0.5 + 1 / 32  # fp32 in, fp32 dequant out, E2M1 nibble, E8M0 byte per 32
+
+
+def make_cfg1_input():
+    """cfg1: 4096x4096 fp32 N(0,1), 0.1% of entries x50, seed 0."""
+    import torch
+
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(4096, 4096, generator=g)
+    idx = torch.randperm(4096 * 4096, generator=g)[:16777]
+    x.view(-1)[idx] *= 50
+    return x
+
+
+def measure_cfg1(dev, steps: int, warmup: int) -> dict:
+    """MXFP4 quantize-dequantize cast of cfg1 with BASELINE's outputs (dequant fp32, packed E2M1
+    codes, E8M0 scale bytes); inputs resident, L2 flushed between launches, CUDA-event timed."""
+    import torch
+
+    from tricast_b200 import quantize_into
+    from tricast_b200.spec import SCHEMES
+
+    x = make_cfg1_input().to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    spec = SCHEMES["mxfp4"]
+    stream = torch.cuda.current_stream(dev)
+
+    def run():
+        return quantize_into(x, spec, want_values=False, want_codes=True, want_scale_codes=True, want_dequant=True)
+
+    for _ in range(warmup):
+        run()
+    times = []
+    for _ in range(steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        run()
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    t = sum(times) / len(times)
+    gbs = x.numel() * CFG1_BYTES_PER_ELEM / (t * 1e-3) / 1e9
+    hbm = measured_peaks().get("hbm_gbs", 6650.0)
+    return {"workload": "cfg1 MXFP4 quantize-dequantize 4096x4096 fp32 (dequant fp32 + packed E2M1 + E8M0 bytes)",
+            "gbs": gbs, "ms": t, "bytes_per_elem": CFG1_BYTES_PER_ELEM, "hbm_frac": gbs / hbm,
+            "hbm_peak_gbs": hbm}
+
+
 def make_inputs(rank: int):
     """Seeded CPU generation so every GPU count sees identical tensors."""
     import torch
@@ -299,6 +348,8 @@ def run_b200(args) -> None:
             "gemm_ms": t_gemm,
             "clocks": clk,
         }
+        if world == 1:
+            line["aux_cast"] = measure_cfg1(dev, args.steps, args.warmup)
         if world == 1 and not args.no_cpu_baseline:
             v, desc = cpu_oracle_sample(32, 512)
             line["cpu_baseline"] = {"value": v, "unit": "GMAC/s", "cores": 1, "kind": "port", "sample": desc}
@@ -315,7 +366,14 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1"],
+                    help="cfg1 runs only the MXFP4 cast measurement (for profiling)")
     args = ap.parse_args()
+    if args.workload == "cfg1" and args.impl != "reference":
+        import torch
+
+        print(json.dumps(measure_cfg1(torch.device("cuda", 0), args.steps, args.warmup)))
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

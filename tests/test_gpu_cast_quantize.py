@@ -200,3 +200,18 @@ def test_noncontiguous_and_amax_override():
     want = oracle_quantize(x.cpu().numpy(), SCHEMES["fp8_tensor"], amax=np.float32(8.0))
     assert bits_equal(got.values.float().cpu().numpy(), want.values)
     assert bits_equal(got.scale.cpu().numpy(), want.scale)
+
+
+@pytest.mark.parametrize("name", ["mxfp4", "nvfp4", "fp8_tensor", "int8_row", "int4_g128_zp"])
+def test_extras_without_values_match(name):
+    """Skipping the QTensor values leaves every other output unchanged (all dispatch paths)."""
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn(64, 256, generator=g).cuda()
+    want_codes = name in ("mxfp4", "nvfp4", "fp8_tensor", "int8_row")
+    q1, e1 = quantize_into(x, SCHEMES[name], want_dequant=True, want_codes=want_codes)
+    q2, e2 = quantize_into(x, SCHEMES[name], want_dequant=True, want_codes=want_codes, want_values=False)
+    assert q2.values is None
+    assert torch.equal(q1.scale, q2.scale)
+    assert bits_equal(e1.dequant.cpu().numpy(), e2.dequant.cpu().numpy())
+    if want_codes:
+        assert torch.equal(e1.codes, e2.codes)

@@ -153,3 +153,34 @@ def test_fp4_fast_path_falls_back_on_specials():
     b = _quantized("mxfp4", 50, 256, 13)
     got = gemm_triton(a, b, spec).cpu().numpy()
     assert bits_equal(got, _oracle_gemm(a, b, spec))
+
+
+@pytest.mark.parametrize("shape", [(37, 70, 200), (1, 1, 5), (130, 65, 1040), (64, 64, 8192)])
+@pytest.mark.parametrize("preset,scheme", [
+    ("nvidia_hopper_fp8", "fp8_tensor"), ("nvidia_ada_fp8", "fp8_tensor"), ("nvidia_hopper_fp8", "mxfp8_e4m3"),
+    ("deepseek_fp8_promote128", "fp8_group128"), ("nvidia_hopper_fp8", "mxfp8_e5m2"),
+])
+def test_cofda_fast_path_vs_oracle(shape, preset, scheme):
+    """The fast CoFDA kernel (epilogue, pow2 product and promoted scales) on ragged shapes."""
+    m, n, k = shape
+    if preset.startswith("deepseek") and k % 128:
+        k = (k // 128 + 1) * 128
+    a = _quantized(scheme, m, k, 21, outliers=min(3, k))
+    b = _quantized(scheme, n, k, 22, scale=0.02)
+    for spec in (PRESETS[preset].with_(out_format="fp32"), PRESETS[preset].with_(norm_rounding="rne", f_bits=9)):
+        got = gemm_triton(a, b, spec).float().cpu().numpy()
+        want = _oracle_gemm(a, b, spec)
+        assert bits_equal(got, want), f"{spec}: {first_mismatch(got, want)}"
+
+
+def test_cofda_chunk8_and_fallback_on_nan():
+    a = _quantized("fp8_tensor", 40, 300, 31)
+    b = _quantized("fp8_tensor", 33, 300, 32, scale=0.02)
+    spec = MMASpec("cofda", f_bits=13, chunk_size=8, out_format="fp32")
+    assert bits_equal(gemm_triton(a, b, spec).cpu().numpy(), _oracle_gemm(a, b, spec))
+    g = torch.Generator().manual_seed(33)
+    x = torch.randn(40, 300, generator=g)
+    x[7, 100] = float("inf")
+    a = as_operand(quantize_triton(x.cuda(), SCHEMES["fp8_row"]))
+    spec = PRESETS["nvidia_hopper_fp8"].with_(out_format="fp32")
+    assert bits_equal(gemm_triton(a, b, spec).cpu().numpy(), _oracle_gemm(a, b, spec))

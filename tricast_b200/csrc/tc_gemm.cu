@@ -139,25 +139,6 @@ __device__ __forceinline__ Term gdfs_group(const GemmDesc &g, int64_t m, int64_t
   return r;
 }
 
-__device__ __forceinline__ float epilogue(const GemmDesc &g, int64_t m, int64_t n, float acc) {
-  if (g.b.skind == SK_TENSOR) acc = __fmul_rn(g.b.scale[0], acc);
-  else if (g.b.skind == SK_ROW) acc = __fmul_rn(g.b.scale[n], acc);
-  if (g.a.skind == SK_TENSOR) acc = __fmul_rn(g.a.scale[0], acc);
-  else if (g.a.skind == SK_ROW) acc = __fmul_rn(g.a.scale[m], acc);
-  if (g.a.alpha || g.b.alpha) {
-    float al = g.a.alpha ? *g.a.alpha : 1.0f;
-    if (g.b.alpha) al = g.a.alpha ? __fmul_rn(al, *g.b.alpha) : *g.b.alpha;
-    acc = __fmul_rn(al, acc);
-  }
-  if (g.bias) acc = __fadd_rn(acc, g.bias[n]);
-  return acc;
-}
-
-__device__ __forceinline__ void store_out(const GemmDesc &g, int64_t m, int64_t n, float acc) {
-  float v = g.out_is_plain ? acc : cast_to(acc, g.of, TC_RNE, false, 0u, 32);
-  store_container(g.out, g.out_dt, m * g.N + n, v);
-}
-
 __global__ void __launch_bounds__(256) gemm_generic_kernel(GemmDesc g, const int32_t *only_if_flag) {
   if (only_if_flag && *only_if_flag == 0) return;  // behind a fast kernel that took the product
   int64_t n = (int64_t)blockIdx.x * 16 + (threadIdx.x & 15);

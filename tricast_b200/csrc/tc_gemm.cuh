@@ -36,6 +36,27 @@ struct GemmDesc {
   void *out;
 };
 
+// Epilogue (src/tricast/reference/mma.py:372-384): tensor/row scales of b then a, alpha_a*alpha_b,
+// bias, each one fp32 RN step, then the out_format rounding into the container.
+__device__ __forceinline__ float epilogue(const GemmDesc &g, int64_t m, int64_t n, float acc) {
+  if (g.b.skind == SK_TENSOR) acc = __fmul_rn(g.b.scale[0], acc);
+  else if (g.b.skind == SK_ROW) acc = __fmul_rn(g.b.scale[n], acc);
+  if (g.a.skind == SK_TENSOR) acc = __fmul_rn(g.a.scale[0], acc);
+  else if (g.a.skind == SK_ROW) acc = __fmul_rn(g.a.scale[m], acc);
+  if (g.a.alpha || g.b.alpha) {
+    float al = g.a.alpha ? *g.a.alpha : 1.0f;
+    if (g.b.alpha) al = g.a.alpha ? __fmul_rn(al, *g.b.alpha) : *g.b.alpha;
+    acc = __fmul_rn(al, acc);
+  }
+  if (g.bias) acc = __fadd_rn(acc, g.bias[n]);
+  return acc;
+}
+
+__device__ __forceinline__ void store_out(const GemmDesc &g, int64_t m, int64_t n, float acc) {
+  float v = g.out_is_plain ? acc : cast_to(acc, g.of, TC_RNE, false, 0u, 32);
+  store_container(g.out, g.out_dt, m * g.N + n, v);
+}
+
 int build_desc(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec, const float *bias, void *out,
                GemmDesc &g);
 

@@ -1,0 +1,470 @@
+// Fast CoFDA kernel for narrow float operands (FP8 / FP6 / FP4 grids), fused accumulator.
+//
+// Reference: TriCast src/tricast/reference/mma.py:286-315 (_cofda) with _fda (:140-151). For a chunk
+// of CS products and running value c, the exact integer FDA at radix F is
+//     total = sum_k sign_k * floor(|a_k b_k| * 2**(F - emax)) + sign_c * floor(|c| * 2**(F - emax))
+// where emax is the largest decoded exponent label (ea + eb for non-zero products, c's normalised
+// exponent): shifting a product significand ma*mb from radix ra+rb to F and then right by emax - e
+// is one floor of its exact value times 2**(F - emax) (two truncating right shifts of a
+// non-negative integer compose into one). The operands' products are exact fp32 values
+// (at most 8 significant bits, exponents well inside fp32's normal range), so each term is
+//     t = fma.rz(P, S, M),  M = copysign(2**23, P),  term = t - M       (S = 2**(F - emax))
+// because |P * S| < 2**(F + 2) <= 2**23 keeps M + P*S inside one binade whose ulp is 1, and
+// round-toward-zero there is the truncation of P*S. With F + 2 + log2(CS + 1) <= 24 every partial
+// sum is an integer below 2**24, so the fp32 additions are exact. Pass 1 (emax) runs as packed
+// 16-bit add-then-max over two outputs per instruction. The exact integer total is normalised by
+// the reference's fixed-point -> fp32 rule (precision min(F, 23), RTZ or RNE, truncating subnormals).
+//
+// This moves the per-product alignment onto the FMA pipe; the integer ALU pipe only carries the
+// sign-magic LOP3 and the packed exponent max.
+//
+// Supported here: c_mode fused, scale_apply epilogue (tensor / row scales, alpha), product with
+// power-of-two K scales (folded into the operands at encode time) and promote (per-interval
+// restart, then fp32 FMA with the interval's K scales). Anything else, and any operand or scale the
+// encoder cannot take (NaN/Inf, off-grid, out-of-range folded scale), goes to the exact generic
+// kernel through the device flag.
+#include <cstring>
+#include <string>
+
+#include "tc_gemm.cuh"
+
+namespace tc {
+namespace cofda {
+
+constexpr int kTile = 64;     // rows of A and columns of B per CTA
+constexpr int kStages = 3;
+constexpr int kZeroExp = -8192;  // exponent label of a zero element (int16)
+
+struct EncodeArgs {
+  const void *v;
+  int dt;
+  int64_t rows, K, rows_pad, nchunks;
+  int CS;
+  Fmt f;
+  const float *scale;  // product-mode pow2 K scales folded into the values, or nullptr
+  int64_t nkd;
+  int kd;
+  Fmt sf;
+  int field0;
+  float *val;          // [tile][chunk][k][kTile]
+  uint32_t *exp;       // A: [tile][chunk][k][kTile/2] (pairs of rows); B: [tile][chunk][k][kTile] (duplicated)
+  int side;
+  int32_t *flag;
+};
+
+__device__ __forceinline__ bool decode_elem(float v, const Fmt &f, int &e) {
+  uint32_t u = f2u(v);
+  uint32_t a = u & 0x7FFFFFFFu;
+  if (a >= kInf) return false;
+  if (a == 0) {
+    e = kZeroExp;
+    return true;
+  }
+  Term t = decode_term(v, f);
+  // On-grid check: the decoded significand must reproduce |v| exactly (mbits <= 3 here).
+  if (t.sig == 0 || t.sig >= (1ull << (f.mbits + 1))) return false;
+  float back = ldexpf((float)t.sig, t.exp - f.mbits);
+  if (back != fabsf(v)) return false;
+  e = t.exp;
+  return true;
+}
+
+__global__ void __launch_bounds__(256) encode_kernel(EncodeArgs e) {
+  const int64_t pairs = e.rows_pad / 2;
+  const int64_t total = pairs * e.nchunks * e.CS;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  bool bad = false;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+    const int64_t rp = idx % (kTile / 2);            // row pair inside the tile
+    int64_t rest = idx / (kTile / 2);
+    const int64_t kk = rest % e.CS;
+    rest /= e.CS;
+    const int64_t chunk = rest % e.nchunks;
+    const int64_t tile = rest / e.nchunks;
+    const int64_t k = chunk * e.CS + kk;
+    float vals[2];
+    int exps[2];
+    for (int h = 0; h < 2; ++h) {
+      const int64_t r = tile * kTile + rp * 2 + h;
+      float v = 0.0f;
+      int ex = kZeroExp;
+      if (r < e.rows && k < e.K) {
+        v = load_as_float(e.v, e.dt, r * e.K + k);
+        if (!decode_elem(v, e.f, ex)) bad = true;
+        if (e.scale) {
+          float s = e.scale[r * e.nkd + k / e.kd];
+          Term ts = decode_term(s, e.sf);
+          bool zero = ts.zero || (e.field0 && f2u(s) == 0x00400000u);
+          if (ts.nan || ts.inf || (!zero && (ts.sig != 1 || ts.neg))) bad = true;  // pow2 scales only
+          if (zero || ex == kZeroExp) {
+            v = 0.0f;
+            ex = kZeroExp;
+          } else {
+            // Keep every folded value inside [2**-60, 2**61) so products stay normal fp32 values.
+            if (ts.exp < -60 || ts.exp > 60 || ex + ts.exp < -60 || ex + ts.exp > 60) bad = true;
+            v = ldexpf(v, ts.exp);
+            ex += ts.exp;
+          }
+        }
+      }
+      if (ex == kZeroExp) v = 0.0f;
+      vals[h] = v;
+      exps[h] = ex;
+    }
+    const int64_t base = ((tile * e.nchunks + chunk) * e.CS + kk) * kTile;
+    e.val[base + rp * 2] = vals[0];
+    e.val[base + rp * 2 + 1] = vals[1];
+    if (e.side == 0) {
+      e.exp[base / 2 + rp] = ((uint32_t)exps[0] & 0xFFFFu) | ((uint32_t)exps[1] << 16);
+    } else {
+      e.exp[base + rp * 2] = ((uint32_t)exps[0] & 0xFFFFu) | ((uint32_t)exps[0] << 16);
+      e.exp[base + rp * 2 + 1] = ((uint32_t)exps[1] & 0xFFFFu) | ((uint32_t)exps[1] << 16);
+    }
+  }
+  if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicExch(e.flag, 1);
+}
+
+struct Args {
+  const float *av, *bv;
+  const uint32_t *ae, *be;
+  int64_t M, N, nchunks, a_tiles_rows, b_tiles_rows;
+  int F, PI_chunks;             // chunks per promote interval (0: no promotion)
+  const float *sa, *sb;          // promote K scales (or nullptr)
+  int64_t sa_nkd, sb_nkd;
+  int sa_kd, sb_kd, CS;
+  GemmDesc g;                    // epilogue (scales, alpha, bias, output)
+  const int32_t *flag;
+  int32_t *status;
+};
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  for (int i = 0; i < (1 << 22); ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
+template <int CS>
+struct Stage {
+  float av[CS][kTile];
+  float bv[CS][kTile];
+  uint32_t be[CS][kTile];
+  uint32_t ae[CS][kTile / 2];
+};
+
+// Normalise an exact int32 fixed-point total (mma.py:118-137, FDA form).
+__device__ __forceinline__ float fixed_to_fp32_i32(int32_t total, int exponent, int radix, bool rne) {
+  return fixed_to_fp32((int64_t)total, exponent, radix, rne, true);
+}
+
+__device__ __forceinline__ int running_exp(float c) {
+  uint32_t a = f2u(c) & 0x7FFFFFFFu;
+  if (a == 0 || a >= kInf) return kZeroExp;
+  uint32_t field = a >> 23;
+  return field ? (int)field - 127 : ilog2_u32(a) - 149;
+}
+
+// The running value as an FDA term at radix F <= 23, aligned to emax with truncation: its 24-bit
+// significand shifted right by (23 - F) + (emax - ec) (mma.py:85-91 then the alignment shift).
+// Exact integer below 2**(F+1), returned as fp32.
+__device__ __forceinline__ float running_term(float c, int F, int emax) {
+  const uint32_t a = f2u(c) & 0x7FFFFFFFu;
+  if (a == 0 || a >= kInf) return 0.0f;
+  const uint32_t field = a >> 23;
+  const uint32_t sig = field ? ((a & 0x7FFFFFu) | 0x800000u) : a;
+  const int lead = ilog2_u32(sig);
+  const int ec = (field ? (int)field - 127 : -126) + lead - 23;
+  const uint32_t norm = sig << (23 - lead);
+  const int sh = (23 - F) + (emax - ec);
+  const uint32_t v = sh >= 32 ? 0u : (norm >> sh);
+  return (f2u(c) >> 31) ? -(float)v : (float)v;
+}
+
+// 2**e as fp32 for e in [-126, 127] (callers clamp).
+__device__ __forceinline__ float pow2f(int e) { return u2f((uint32_t)(e + 127) << 23); }
+
+// floor(|x| * s) with x's sign, exact for |x * s| < 2**23 (x * s exact or not).
+__device__ __forceinline__ float trunc_scaled(float x, float s) {
+  const float m = u2f((f2u(x) & 0x80000000u) | 0x4B000000u);
+  return __fadd_rn(__fmaf_rz(x, s, m), -m);
+}
+
+template <int CS, bool RNE>
+__global__ void __launch_bounds__(256) cofda_kernel(Args p) {
+  if (*p.flag) return;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  Stage<CS> *stages = reinterpret_cast<Stage<CS> *>(smem_raw);
+  __shared__ __align__(8) uint64_t full[kStages];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t mt = blockIdx.y, nt = blockIdx.x;
+  const int64_t m0 = mt * kTile, n0 = nt * kTile;
+  constexpr uint32_t kValBytes = CS * kTile * 4;
+  constexpr uint32_t kAexpBytes = CS * (kTile / 2) * 4;
+  constexpr uint32_t kStageBytes = 3 * kValBytes + kAexpBytes;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  auto issue = [&](int64_t c, int s) {
+    Stage<CS> &st = stages[s];
+    mbar_expect_tx(&full[s], kStageBytes);
+    const int64_t a_off = (mt * p.nchunks + c) * CS * kTile;
+    const int64_t b_off = (nt * p.nchunks + c) * CS * kTile;
+    bulk_g2s(&st.av[0][0], p.av + a_off, kValBytes, &full[s]);
+    bulk_g2s(&st.ae[0][0], p.ae + a_off / 2, kAexpBytes, &full[s]);
+    bulk_g2s(&st.bv[0][0], p.bv + b_off, kValBytes, &full[s]);
+    bulk_g2s(&st.be[0][0], p.be + b_off, kValBytes, &full[s]);
+  };
+  if (threadIdx.x == 0)
+    for (int s = 0; s < kStages && s < p.nchunks; ++s) issue(s, s);
+
+  float c[4][4], acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) c[i][j] = acc[i][j] = 0.0f;
+
+  const int F = p.F;
+  bool timed_out = false;
+  for (int64_t ch = 0; ch < p.nchunks; ++ch) {
+    const int s = (int)(ch % kStages);
+    if (!mbar_wait(&full[s], (uint32_t)((ch / kStages) & 1))) timed_out = true;
+    if (__syncthreads_or(timed_out)) {
+      if (threadIdx.x == 0) atomicExch(p.status, 1);
+      return;
+    }
+    const Stage<CS> &st = stages[s];
+    // Pass 1: emax over two rows at once (16-bit halves).
+    uint32_t em2[2][4];
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        em2[q][j] = ((uint32_t)running_exp(c[2 * q][j]) & 0xFFFFu) | ((uint32_t)running_exp(c[2 * q + 1][j]) << 16);
+#pragma unroll 8
+    for (int kk = 0; kk < CS; ++kk) {
+      const uint2 ea = *reinterpret_cast<const uint2 *>(&st.ae[kk][ty * 2]);
+      const uint4 eb = *reinterpret_cast<const uint4 *>(&st.be[kk][tx * 4]);
+      const uint32_t ebs[4] = {eb.x, eb.y, eb.z, eb.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        em2[0][j] = __viaddmax_s16x2(ea.x, ebs[j], em2[0][j]);
+        em2[1][j] = __viaddmax_s16x2(ea.y, ebs[j], em2[1][j]);
+      }
+    }
+    int emax[4][4];
+    float S[4][4], tot[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t w = em2[i >> 1][j];
+        emax[i][j] = (int)(int16_t)((i & 1) ? (w >> 16) : (w & 0xFFFFu));
+        int se = F - emax[i][j];
+        se = se > 127 ? 127 : (se < -126 ? -126 : se);
+        S[i][j] = pow2f(se);
+        tot[i][j] = running_term(c[i][j], F, emax[i][j]);
+      }
+    // Pass 2: exact aligned sum.
+#pragma unroll 4
+    for (int kk = 0; kk < CS; ++kk) {
+      const float4 a = *reinterpret_cast<const float4 *>(&st.av[kk][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4 *>(&st.bv[kk][tx * 4]);
+      const float as[4] = {a.x, a.y, a.z, a.w};
+      const float bs[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tot[i][j] = __fadd_rn(tot[i][j], trunc_scaled(__fmul_rn(as[i], bs[j]), S[i][j]));
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
+        if (cb >= kInf) continue;  // an overflowed running value is sticky (operands are finite)
+        const int32_t t = (int32_t)tot[i][j];
+        c[i][j] = t == 0 ? 0.0f : fixed_to_fp32_i32(t, emax[i][j], F, RNE);
+      }
+    if (p.PI_chunks && (ch + 1) % p.PI_chunks == 0 || p.PI_chunks && ch + 1 == p.nchunks) {
+      // End of a promote interval: acc = fma(partial, (1 * sa) * sb, acc), partial restarts at 0.
+      const int64_t begin = (ch / p.PI_chunks) * (int64_t)p.PI_chunks * CS;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int64_t m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
+          float w = 1.0f;
+          if (p.sa && m < p.M) w = __fmul_rn(w, p.sa[m * p.sa_nkd + begin / p.sa_kd]);
+          if (p.sb && n < p.N) w = __fmul_rn(w, p.sb[n * p.sb_nkd + begin / p.sb_kd]);
+          acc[i][j] = __fmaf_rn(c[i][j], w, acc[i][j]);
+          c[i][j] = 0.0f;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && ch + kStages < p.nchunks) issue(ch + kStages, s);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
+      if (m >= p.M || n >= p.N) continue;
+      store_out(p.g, m, n, epilogue(p.g, m, n, p.PI_chunks ? acc[i][j] : c[i][j]));
+    }
+}
+
+}  // namespace cofda
+
+// ---------------------------------------------------------------- dispatch
+struct CofdaPlan {
+  bool ok;
+  int CS;
+  int64_t nchunks, a_pad, b_pad;
+  size_t off[4], total, flag_off;
+};
+
+static bool narrow_float(const Fmt &f) { return f.kind == 0 && f.mbits <= 3 && f.emax <= 15 && f.emin >= -14; }
+
+static CofdaPlan plan_cofda(const GemmDesc &g) {
+  CofdaPlan p;
+  std::memset(&p, 0, sizeof(p));
+  if (g.alg != ALG_COFDA || g.decoupled) return p;
+  if (g.CS != 8 && g.CS != 16 && g.CS != 32) return p;
+  if (!narrow_float(g.a.f) || !narrow_float(g.b.f)) return p;
+  int width_bits = 0;
+  while ((1 << width_bits) <= g.CS) ++width_bits;  // bit length of CS (covers CS + 1 terms)
+  if (g.F + 2 + width_bits > 24) return p;
+  if (g.apply == AP_PRODUCT) {
+    for (const OpDesc *o : {&g.a, &g.b})
+      if (o->skind == SK_K && o->sf.kind != 2) return p;  // only power-of-two product scales fold
+  } else if (g.apply == AP_PROMOTE) {
+    if (g.PI <= 0 || g.PI % g.CS) return p;
+  } else if (g.apply != AP_EPILOGUE) {
+    return p;
+  }
+  if (g.apply != AP_PROMOTE && g.PI) return p;
+  p.CS = g.CS;
+  p.nchunks = (g.K + g.CS - 1) / g.CS;
+  p.a_pad = (g.M + cofda::kTile - 1) / cofda::kTile * cofda::kTile;
+  p.b_pad = (g.N + cofda::kTile - 1) / cofda::kTile * cofda::kTile;
+  const size_t ka = (size_t)p.a_pad * p.nchunks * g.CS, kb = (size_t)p.b_pad * p.nchunks * g.CS;
+  size_t sizes[4] = {ka * 4, ka * 2, kb * 4, kb * 4};
+  size_t off = 0;
+  for (int i = 0; i < 4; ++i) {
+    p.off[i] = off;
+    off += (sizes[i] + 255) & ~(size_t)255;
+  }
+  p.flag_off = off;
+  p.total = off + 256;
+  p.ok = true;
+  return p;
+}
+
+size_t cofda_workspace(const GemmDesc &g) {
+  CofdaPlan p = plan_cofda(g);
+  return p.ok ? p.total : 0;
+}
+
+template <int CS, bool RNE>
+static int launch_cofda_kernel(const cofda::Args &a, cudaStream_t s) {
+  size_t smem = sizeof(cofda::Stage<CS>) * cofda::kStages;
+  cudaError_t e = cudaFuncSetAttribute(cofda::cofda_kernel<CS, RNE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return set_error(std::string("cofda: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
+  dim3 grid((unsigned)((a.N + cofda::kTile - 1) / cofda::kTile), (unsigned)((a.M + cofda::kTile - 1) / cofda::kTile));
+  cofda::cofda_kernel<CS, RNE><<<grid, 256, smem, s>>>(a);
+  count_launch();
+  return TC_OK;
+}
+
+int launch_cofda(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s) {
+  CofdaPlan p = plan_cofda(g);
+  if (!p.ok) return TC_UNSUPPORTED;
+  if (!workspace || workspace_bytes < p.total) return set_error("tc_gemm: workspace too small"), TC_WORKSPACE_TOO_SMALL;
+  if ((g.M + cofda::kTile - 1) / cofda::kTile > 65535) return TC_UNSUPPORTED;
+  char *ws = static_cast<char *>(workspace);
+  int32_t *flag = reinterpret_cast<int32_t *>(ws + p.flag_off);
+  cudaMemsetAsync(flag, 0, 2 * sizeof(int32_t), s);
+  for (int side = 0; side < 2; ++side) {
+    const OpDesc &o = side ? g.b : g.a;
+    cofda::EncodeArgs e;
+    std::memset(&e, 0, sizeof(e));
+    e.v = o.v;
+    e.dt = o.dt;
+    e.rows = o.rows;
+    e.K = o.K;
+    e.rows_pad = side ? p.b_pad : p.a_pad;
+    e.nchunks = p.nchunks;
+    e.CS = p.CS;
+    e.f = o.f;
+    e.scale = (g.apply == AP_PRODUCT && o.skind == SK_K) ? o.scale : nullptr;
+    e.nkd = o.nkd;
+    e.kd = o.kd;
+    e.sf = o.sf;
+    e.field0 = o.field0;
+    e.val = reinterpret_cast<float *>(ws + p.off[side * 2]);
+    e.exp = reinterpret_cast<uint32_t *>(ws + p.off[side * 2 + 1]);
+    e.side = side;
+    e.flag = flag;
+    int64_t work = (e.rows_pad / 2) * p.nchunks * p.CS;
+    int64_t blocks = (work + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    cofda::encode_kernel<<<(unsigned)blocks, 256, 0, s>>>(e);
+    count_launch();
+  }
+  cofda::Args a;
+  std::memset(&a, 0, sizeof(a));
+  a.av = reinterpret_cast<const float *>(ws + p.off[0]);
+  a.ae = reinterpret_cast<const uint32_t *>(ws + p.off[1]);
+  a.bv = reinterpret_cast<const float *>(ws + p.off[2]);
+  a.be = reinterpret_cast<const uint32_t *>(ws + p.off[3]);
+  a.M = g.M;
+  a.N = g.N;
+  a.nchunks = p.nchunks;
+  a.F = g.F;
+  a.CS = p.CS;
+  a.PI_chunks = g.apply == AP_PROMOTE ? g.PI / g.CS : 0;
+  if (g.apply == AP_PROMOTE) {
+    if (g.a.skind == SK_K) { a.sa = g.a.scale; a.sa_nkd = g.a.nkd; a.sa_kd = g.a.kd; }
+    if (g.b.skind == SK_K) { a.sb = g.b.scale; a.sb_nkd = g.b.nkd; a.sb_kd = g.b.kd; }
+  }
+  a.g = g;
+  a.flag = flag;
+  a.status = flag + 1;
+  int st;
+  if (p.CS == 32) st = g.rne ? launch_cofda_kernel<32, true>(a, s) : launch_cofda_kernel<32, false>(a, s);
+  else if (p.CS == 16) st = g.rne ? launch_cofda_kernel<16, true>(a, s) : launch_cofda_kernel<16, false>(a, s);
+  else st = g.rne ? launch_cofda_kernel<8, true>(a, s) : launch_cofda_kernel<8, false>(a, s);
+  if (st) return st;
+  launch_generic(g, flag, s);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(std::string("tc_gemm cofda: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
+  return TC_OK;
+}
+
+}  // namespace tc

@@ -420,9 +420,13 @@ static Fp4Plan plan_fp4(const GemmDesc &g) {
   return p;
 }
 
+size_t cofda_workspace(const GemmDesc &g);
+int launch_cofda(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
+
 size_t fast_workspace(const GemmDesc &g) {
   Fp4Plan p = plan_fp4(g);
-  return p.ok ? p.total : 0;
+  if (p.ok) return p.total;
+  return cofda_workspace(g);
 }
 
 template <int NG>
@@ -438,7 +442,7 @@ static int launch_fp4_gemm(const fp4::GemmArgs &args, int64_t M, int64_t N, cuda
 
 int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s) {
   Fp4Plan p = plan_fp4(g);
-  if (!p.ok) return TC_UNSUPPORTED;
+  if (!p.ok) return launch_cofda(g, workspace, workspace_bytes, s);
   if (!workspace || workspace_bytes < p.total) return set_error("tc_gemm: workspace too small"), TC_WORKSPACE_TOO_SMALL;
   if (p.ntiles * fp4::kTileRows > (int64_t)1 << 40) return TC_UNSUPPORTED;
   char *ws = static_cast<char *>(workspace);

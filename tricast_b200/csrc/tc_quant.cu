@@ -35,8 +35,8 @@ struct QParams {
   int x_dtype, v_dtype;
   int code_bits;            // 0, 4 or 8
   int scode;                // 0 none, 1 byte code of the scale format
-  float prod_max;           // element max * scale max (two-level), only its double below is used
-  double prod_max_d;
+  double prod_max_d;        // element max * scale max (two-level global scale)
+  int pow2_div;             // every divisor is a power of two (pow2 methods, one level)
 };
 
 // ------------------------------------------------------------------ element codes
@@ -201,14 +201,26 @@ struct ElemOut {
   float dequant;
 };
 
-__device__ __forceinline__ ElemOut quant_elem(float x, float s, float z, float d2, bool has_d2, const QParams &p,
-                                              uint32_t noise) {
+// The divisor of a domain: s (one level) or RN(s * d2) (two-level), and, when it is a power of two,
+// its exact reciprocal: RN(x / 2**e) == RN(x * 2**-e) for every fp32 x, 2**-e being representable.
+struct Divisor {
+  float eff, inv;
+  bool by_inv;
+};
+
+__device__ __forceinline__ Divisor make_divisor(float s, float d2, bool has_d2, const QParams &p) {
+  Divisor d;
+  d.eff = has_d2 ? __fmul_rn(s, d2) : s;
+  d.by_inv = p.pow2_div != 0;
+  d.inv = d.by_inv ? __frcp_rn(d.eff) : 0.0f;
+  return d;
+}
+
+__device__ __forceinline__ ElemOut quant_elem_d(float x, float s, float z, const Divisor &dv, float d2, bool has_d2,
+                                                const QParams &p, uint32_t noise) {
   float xq = x;
   if (p.zp == ZP_FLOAT) xq = __fsub_rn(xq, z);
-  if (p.has_scale) {
-    float eff = has_d2 ? __fmul_rn(s, d2) : s;
-    xq = __fdiv_rn(xq, eff);
-  }
+  if (p.has_scale) xq = dv.by_inv ? __fmul_rn(xq, dv.inv) : __fdiv_rn(xq, dv.eff);
   ElemOut o;
   o.value = p.zp ? zp_round(xq, z, p, noise) : cast_to(xq, p.ef, p.rnd, p.saturate, noise, p.sr_bits);
   float d = o.value;
@@ -218,6 +230,11 @@ __device__ __forceinline__ ElemOut quant_elem(float x, float s, float z, float d
   if (has_d2) d = __fmul_rn(d, d2);
   o.dequant = d;
   return o;
+}
+
+__device__ __forceinline__ ElemOut quant_elem(float x, float s, float z, float d2, bool has_d2, const QParams &p,
+                                              uint32_t noise) {
+  return quant_elem_d(x, s, z, make_divisor(s, d2, has_d2, p), d2, has_d2, p, noise);
 }
 
 // ------------------------------------------------------------------ cast kernel
@@ -417,7 +434,7 @@ __global__ void __launch_bounds__(256) element_kernel(const void *__restrict__ x
         if (p.zp) z = zero[d];
       }
       ElemOut o = quant_elem(load_as_float(x, p.x_dtype, i), s, z, d2, p.two_level, p, noise ? noise[i] : 0u);
-      store_container(values, p.v_dtype, i, o.value);
+      if (values) store_container(values, p.v_dtype, i, o.value);
       if (dequant) dequant[i] = o.dequant;
       if (codes) cc[j] = element_code(o.value, p.ef, p.code_bits == 4 ? 4 : 8);
     }
@@ -495,13 +512,15 @@ __global__ void __launch_bounds__(256) group_kernel(const void *__restrict__ x, 
       for (int j = 0; j < 4; ++j) nn[j] = noise[i0 + j];
     float q[4], dq[4];
     uint32_t cd[4];
+    const Divisor dv = make_divisor(sc, d2, p.two_level, p);
     for (int j = 0; j < 4; ++j) {
-      ElemOut o = quant_elem(v[j], sc, z, d2, p.two_level, p, nn[j]);
+      ElemOut o = quant_elem_d(v[j], sc, z, dv, d2, p.two_level, p, nn[j]);
       q[j] = o.value;
       dq[j] = o.dequant;
       cd[j] = codes ? element_code(o.value, p.ef, p.code_bits == 4 ? 4 : 8) : 0u;
     }
-    if (p.v_dtype == TC_F32) {
+    if (!values) {
+    } else if (p.v_dtype == TC_F32) {
       *reinterpret_cast<float4 *>(static_cast<float *>(values) + i0) = make_float4(q[0], q[1], q[2], q[3]);
     } else {
       uint16_t h[4];
@@ -526,6 +545,187 @@ __global__ void __launch_bounds__(256) group_kernel(const void *__restrict__ x, 
   }
 }
 
+// ------------------------------------------------------------------ tensor statistics
+// One Stat for the whole tensor, reduced with atomics into a workspace slot that the host cleared
+// to the identity (amax 0, lo 0xFFFFFFFF, hi 0, nan 0). 16-byte loads when aligned.
+__global__ void __launch_bounds__(256) tensor_stats_kernel(const void *__restrict__ x, int dt, int64_t n, int vec,
+                                                           Stat *__restrict__ out) {
+  Stat s;
+  stat_init(s);
+  int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t done = 0;
+  if (vec && dt == TC_F32) {
+    int64_t n4 = n >> 2;
+    for (int64_t i = tid; i < n4; i += stride) {
+      float4 v = reinterpret_cast<const float4 *>(x)[i];
+      stat_add(s, v.x); stat_add(s, v.y); stat_add(s, v.z); stat_add(s, v.w);
+    }
+    done = n4 << 2;
+  } else if (vec) {
+    int64_t n8 = n >> 3;
+    for (int64_t i = tid; i < n8; i += stride) {
+      uint4 u = reinterpret_cast<const uint4 *>(x)[i];
+      uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      for (int j = 0; j < 4; ++j) {
+        uint16_t lo = (uint16_t)(w[j] & 0xFFFF), hi = (uint16_t)(w[j] >> 16);
+        if (dt == TC_BF16) {
+          stat_add(s, __bfloat162float(__ushort_as_bfloat16(lo)));
+          stat_add(s, __bfloat162float(__ushort_as_bfloat16(hi)));
+        } else {
+          stat_add(s, __half2float(__ushort_as_half(lo)));
+          stat_add(s, __half2float(__ushort_as_half(hi)));
+        }
+      }
+    }
+    done = n8 << 3;
+  }
+  for (int64_t i = done + tid; i < n; i += stride) stat_add(s, load_as_float(x, dt, i));
+  for (int m = 16; m; m >>= 1) stat_merge(s, stat_shfl(s, m));
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(&out->amax, s.amax);
+    atomicMin(&out->lo, s.lo);
+    atomicMax(&out->hi, s.hi);
+    if (s.nan) atomicExch(&out->nan, 1u);
+  }
+}
+
+// ------------------------------------------------------------------ row-resident pass
+// Granularity "row": one block per row (grid-stride over rows). Pass 1 reduces the row's statistic,
+// thread 0 derives the scale, pass 2 re-reads the row (now in L1/L2) and writes every output.
+__global__ void __launch_bounds__(256) row_kernel(const void *__restrict__ x, QParams p,
+                                                  const float *__restrict__ d2p, const uint32_t *__restrict__ noise,
+                                                  const uint32_t *__restrict__ scale_noise, void *__restrict__ values,
+                                                  float *__restrict__ scale, float *__restrict__ zero,
+                                                  uint8_t *__restrict__ codes, uint8_t *__restrict__ scodes,
+                                                  float *__restrict__ dequant) {
+  __shared__ Stat warp_stat[8];
+  __shared__ float sh_scale, sh_zero;
+  const float d2 = p.two_level ? *d2p : 1.0f;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t r = blockIdx.x; r < p.rows; r += gridDim.x) {
+    const int64_t base = r * p.K;
+    Stat s;
+    stat_init(s);
+    for (int64_t c = threadIdx.x; c < p.K; c += blockDim.x) stat_add(s, load_as_float(x, p.x_dtype, base + c));
+    for (int m = 16; m; m >>= 1) stat_merge(s, stat_shfl(s, m));
+    if (lane == 0) warp_stat[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w) stat_merge(s, warp_stat[w]);
+      uint32_t sn = scale_noise ? scale_noise[r] : 0u;
+      float sc, z = 0.0f;
+      if (p.zp) {
+        float lo = s.nan ? u2f(kQNaN) : unkey(s.lo);
+        float hi = s.nan ? u2f(kQNaN) : unkey(s.hi);
+        zp_scale(lo, hi, p, sn, sc, z);
+        zero[r] = z;
+      } else if (p.two_level || p.method == M_ABSMAX) {
+        sc = amax_scale(u2f(s.amax), d2, p.two_level, p, sn);
+      } else {
+        sc = pow2_scale(u2f(s.amax), p);
+      }
+      scale[r] = sc;
+      if (scodes) scodes[r] = (uint8_t)scale_code(sc, p.sf);
+      sh_scale = sc;
+      sh_zero = z;
+    }
+    __syncthreads();
+    const float sc = sh_scale, z = sh_zero;
+    const Divisor dv = make_divisor(sc, d2, p.two_level, p);
+    // Pairs of elements so 4-bit codes pack into whole bytes (K even is required for codes).
+    for (int64_t c = 2 * threadIdx.x; c < p.K; c += 2 * blockDim.x) {
+      uint32_t cc[2] = {0, 0};
+      for (int j = 0; j < 2 && c + j < p.K; ++j) {
+        int64_t i = base + c + j;
+        ElemOut o = quant_elem_d(load_as_float(x, p.x_dtype, i), sc, z, dv, d2, p.two_level, p,
+                                 noise ? noise[i] : 0u);
+        if (values) store_container(values, p.v_dtype, i, o.value);
+        if (dequant) dequant[i] = o.dequant;
+        if (codes) cc[j] = element_code(o.value, p.ef, p.code_bits == 4 ? 4 : 8);
+      }
+      if (codes) {
+        if (p.code_bits == 8) {
+          codes[base + c] = (uint8_t)cc[0];
+          if (c + 1 < p.K) codes[base + c + 1] = (uint8_t)cc[1];
+        } else {
+          codes[(base + c) >> 1] = (uint8_t)((cc[0] & 0xF) | ((cc[1] & 0xF) << 4));
+        }
+      }
+    }
+    __syncthreads();  // warp_stat / sh_scale are reused by the next row
+  }
+}
+
+// One thread: the scale (or d2) of a single-domain spec from the reduced tensor statistic.
+__global__ void tensor_scale_kernel(QParams p, const Stat *__restrict__ st, const float *__restrict__ amax_override,
+                                    float *__restrict__ d2_slot, const uint32_t *__restrict__ scale_noise,
+                                    float *__restrict__ scale, float *__restrict__ zero, uint8_t *__restrict__ scodes,
+                                    int global_only) {
+  Stat s = *st;
+  float amax = amax_override ? *amax_override : u2f(s.amax);
+  if (global_only) {
+    *d2_slot = global_scale(amax, p.prod_max_d);
+    return;
+  }
+  uint32_t noise = scale_noise ? scale_noise[0] : 0u;
+  float sc, z = 0.0f;
+  if (p.zp) {
+    float lo = s.nan ? u2f(kQNaN) : unkey(s.lo);
+    float hi = s.nan ? u2f(kQNaN) : unkey(s.hi);
+    zp_scale(lo, hi, p, noise, sc, z);
+    zero[0] = z;
+  } else if (p.two_level || p.method == M_ABSMAX) {
+    sc = amax_scale(amax, p.two_level ? *d2_slot : 1.0f, p.two_level, p, noise);
+  } else {
+    sc = pow2_scale(amax, p);
+  }
+  scale[0] = sc;
+  if (scodes) scodes[0] = (uint8_t)scale_code(sc, p.sf);
+}
+
+// Elements of a single-domain (tensor) spec, or of a direct cast: 4 consecutive elements per thread.
+__global__ void __launch_bounds__(256) flat_kernel(const void *__restrict__ x, QParams p,
+                                                   const float *__restrict__ scale, const float *__restrict__ zero,
+                                                   const float *__restrict__ d2p, const uint32_t *__restrict__ noise,
+                                                   void *__restrict__ values, uint8_t *__restrict__ codes,
+                                                   float *__restrict__ dequant) {
+  const int64_t n = p.rows * p.K;
+  const float d2 = p.two_level ? *d2p : 1.0f;
+  const float sc = p.has_scale ? scale[0] : 1.0f;
+  const float z = p.zp ? zero[0] : 0.0f;
+  const Divisor dv = make_divisor(sc, d2, p.two_level, p);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q * 4 < n; q += stride) {
+    const int64_t i0 = q * 4;
+    float v[4];
+    const bool full = i0 + 4 <= n;
+    if (full && p.x_dtype == TC_F32 && (((uintptr_t)x & 15) == 0)) {
+      float4 t = reinterpret_cast<const float4 *>(x)[q];
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+      for (int j = 0; j < 4; ++j) v[j] = i0 + j < n ? load_as_float(x, p.x_dtype, i0 + j) : 0.0f;
+    }
+    float o[4], dq[4];
+    uint32_t cd[4] = {0, 0, 0, 0};
+    for (int j = 0; j < 4; ++j) {
+      ElemOut e = quant_elem_d(v[j], sc, z, dv, d2, p.two_level, p, noise && i0 + j < n ? noise[i0 + j] : 0u);
+      o[j] = e.value;
+      dq[j] = e.dequant;
+      if (codes) cd[j] = element_code(e.value, p.ef, p.code_bits == 4 ? 4 : 8);
+    }
+    for (int j = 0; j < 4 && i0 + j < n; ++j) {
+      if (values) store_container(values, p.v_dtype, i0 + j, o[j]);
+      if (dequant) dequant[i0 + j] = dq[j];
+      if (codes && p.code_bits == 8) codes[i0 + j] = (uint8_t)cd[j];
+    }
+    if (codes && p.code_bits == 4) {
+      codes[i0 >> 1] = (uint8_t)((cd[0] & 0xF) | ((cd[1] & 0xF) << 4));
+      if (i0 + 2 < n) codes[(i0 >> 1) + 1] = (uint8_t)((cd[2] & 0xF) | ((cd[3] & 0xF) << 4));
+    }
+  }
+}
+
 // ------------------------------------------------------------------ host side
 static int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
@@ -535,13 +735,14 @@ static int stats_parts(int64_t domain_elems) {
   return (int)(parts < 1 ? 1 : parts);
 }
 
+enum { PATH_FLAT = 0, PATH_GROUP = 1, PATH_ROW = 2, PATH_TENSOR = 3, PATH_GENERAL = 4 };
+
 struct Plan {
   QParams p;
   int64_t nd;
   int parts;          // per-domain partials of the general path
-  int tensor_parts;   // partials of the tensor-amax pre-pass
-  bool fused;
-  size_t ws_stats, ws_tensor, ws_d2, total;
+  int path;
+  size_t ws_stats, total;  // general-path partials; plus one tensor Stat slot
 };
 
 static int make_plan(const void *x, int32_t x_dtype, int64_t rows, int64_t K, const tc_quant_spec *spec,
@@ -588,6 +789,8 @@ static int make_plan(const void *x, int32_t x_dtype, int64_t rows, int64_t K, co
     if (spec->zero_point) return set_error("zero points need a scale"), TC_INVALID_ARGUMENT;
     p.dr = rows; p.dc = K; p.nr = 1; p.nc = 1;
     pl.nd = 0;
+    pl.path = PATH_FLAT;
+    pl.total = 256;
     return TC_OK;
   }
   err = fmt_error(spec->scale_format);
@@ -627,18 +830,22 @@ static int make_plan(const void *x, int32_t x_dtype, int64_t rows, int64_t K, co
   p.nr = cdiv(rows, p.dr);
   p.nc = cdiv(K, p.dc);
   pl.nd = p.nr * p.nc;
+  // Power-of-two divisors (one-level pow2 methods) are applied by an exact reciprocal multiply.
+  p.pow2_div = !p.two_level && !p.zp && (p.method == M_POW2_FLOOR || p.method == M_POW2_CEIL);
   int gs = (int)p.dc;
   bool aligned = ((uintptr_t)x % (x_dtype == TC_F32 ? 16 : 8)) == 0;
-  pl.fused = spec->granularity == GRAN_GROUP && p.dr == 1 && K % gs == 0 && gs % 4 == 0 &&
-             (gs == 4 || gs == 8 || gs == 16 || gs == 32 || gs == 64 || gs == 128) && aligned &&
-             ((uintptr_t)out->values % 16) == 0 && (!out->dequant || ((uintptr_t)out->dequant % 16) == 0) &&
-             (!out->codes || ((uintptr_t)out->codes % 4) == 0);
+  bool group_ok = spec->granularity == GRAN_GROUP && p.dr == 1 && K % gs == 0 && gs % 4 == 0 &&
+                  (gs == 4 || gs == 8 || gs == 16 || gs == 32 || gs == 64 || gs == 128) && aligned &&
+                  (!out->values || ((uintptr_t)out->values % 16) == 0) &&
+                  (!out->dequant || ((uintptr_t)out->dequant % 16) == 0) &&
+                  (!out->codes || ((uintptr_t)out->codes % 4) == 0);
+  if (group_ok) pl.path = PATH_GROUP;
+  else if (p.dr == 1 && p.dc == K && (!out->codes || p.code_bits == 8 || K % 2 == 0)) pl.path = PATH_ROW;
+  else if (p.nr == 1 && p.nc == 1) pl.path = PATH_TENSOR;
+  else pl.path = PATH_GENERAL;
   pl.parts = stats_parts(p.dr * p.dc);
-  pl.tensor_parts = stats_parts(rows * K);
-  pl.ws_stats = pl.fused ? 0 : sizeof(Stat) * (size_t)pl.nd * pl.parts;
-  pl.ws_tensor = p.two_level ? sizeof(Stat) * (size_t)pl.tensor_parts : 0;
-  pl.ws_d2 = 0;
-  pl.total = ((pl.ws_stats + 255) & ~(size_t)255) + ((pl.ws_tensor + 255) & ~(size_t)255);
+  pl.ws_stats = pl.path == PATH_GENERAL ? sizeof(Stat) * (size_t)pl.nd * pl.parts : 0;
+  pl.total = ((pl.ws_stats + 255) & ~(size_t)255) + 256;
   return TC_OK;
 }
 
@@ -669,17 +876,19 @@ extern "C" size_t tc_quantize_workspace(int64_t rows, int64_t K, const tc_quant_
   Plan pl;
   tc_quant_out dummy;
   std::memset(&dummy, 0, sizeof(dummy));
-  // Alignment-independent upper bound: assume the general pass.
+  // Upper bound independent of pointer alignment: size the general path's partials as well.
   static float probe[4] __attribute__((aligned(16)));
-  if (make_plan(probe, TC_F32, rows, K, spec, &dummy, pl) != TC_OK) return 0;
-  size_t stats = sizeof(Stat) * (size_t)pl.nd * pl.parts;
-  return ((stats + 255) & ~(size_t)255) + ((pl.ws_tensor + 255) & ~(size_t)255);
+  if (make_plan(probe, TC_F32, rows, K, spec, &dummy, pl) != TC_OK) return 256;
+  size_t stats = pl.nd ? sizeof(Stat) * (size_t)pl.nd * pl.parts : 0;
+  return ((stats + 255) & ~(size_t)255) + 256;
 }
 
 extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t K, const tc_quant_spec *spec,
                            const float *amax, const uint32_t *noise, const uint32_t *scale_noise,
                            const tc_quant_out *out, void *workspace, size_t workspace_bytes, tc_stream stream) {
-  if (!x || !spec || !out || !out->values) return set_error("tc_quantize: null argument"), TC_INVALID_ARGUMENT;
+  if (!x || !spec || !out) return set_error("tc_quantize: null argument"), TC_INVALID_ARGUMENT;
+  if (!out->values && !out->codes && !out->dequant)
+    return set_error("tc_quantize: no element output (values, codes or dequant)"), TC_INVALID_ARGUMENT;
   Plan pl;
   int st = make_plan(x, x_dtype, rows, K, spec, out, pl);
   if (st) return st;
@@ -688,47 +897,43 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
     return set_error("tc_quantize: missing scale / zero_point / global_scale output"), TC_INVALID_ARGUMENT;
   if (amax && spec->granularity != GRAN_TENSOR)
     return set_error("amax override requires tensor granularity and a scalar"), TC_INVALID_ARGUMENT;
-  if (pl.total > workspace_bytes)
+  if (pl.total > workspace_bytes || !workspace)
     return set_error("tc_quantize: workspace too small"), TC_WORKSPACE_TOO_SMALL;
   cudaStream_t s = (cudaStream_t)stream;
   char *ws = static_cast<char *>(workspace);
   Stat *stats = reinterpret_cast<Stat *>(ws);
-  Stat *tstats = reinterpret_cast<Stat *>(ws + ((pl.ws_stats + 255) & ~(size_t)255));
+  Stat *tstat = reinterpret_cast<Stat *>(ws + ((pl.ws_stats + 255) & ~(size_t)255));
   float *d2 = out->global_scale;
-  int64_t n = rows * K;
-  if (!p.has_scale) {
-    element_kernel<<<grid_for((n + 1) / 2, 256), 256, 0, s>>>(x, p, nullptr, nullptr, nullptr, noise, out->values,
+  const int64_t n = rows * K;
+  const int vec = ((uintptr_t)x % 16) == 0;
+  if (pl.path == PATH_FLAT) {
+    flat_kernel<<<grid_for((n + 3) / 4, 256, 8), 256, 0, s>>>(x, p, nullptr, nullptr, nullptr, noise, out->values,
                                                              out->codes, out->dequant);
     ::tc::count_launch();
     return launch_status("tc_quantize elements");
   }
-  if (p.two_level) {
-    if (amax) {
-      // d2 from the override: one warp, no partials.
-      QParams q = p;
-      scale_kernel<<<1, 32, 0, s>>>(q, 1, 0, tstats, amax, d2, nullptr, nullptr, nullptr, nullptr, 1);
-      ::tc::count_launch();
-    } else {
-      QParams q = p;
-      q.dr = rows; q.dc = K; q.nr = 1; q.nc = 1;
-      int64_t chunk = cdiv(n, pl.tensor_parts);
-      stats_kernel<<<pl.tensor_parts, 256, 0, s>>>(x, q, 1, pl.tensor_parts, chunk, tstats);
-      ::tc::count_launch();
-      scale_kernel<<<1, 32, 0, s>>>(q, 1, pl.tensor_parts, tstats, nullptr, d2, nullptr, nullptr, nullptr, nullptr, 1);
-      ::tc::count_launch();
-    }
-    if ((st = launch_status("tc_quantize global scale"))) return st;
+  // Tensor statistic: needed for two-level d2, and as the single domain of tensor granularity.
+  const bool need_tensor_stat = (p.two_level || pl.path == PATH_TENSOR) && !(amax && !p.zp);
+  if (need_tensor_stat) {
+    cudaMemsetAsync(tstat, 0, sizeof(Stat), s);
+    cudaMemsetAsync(&tstat->lo, 0xFF, sizeof(uint32_t), s);
+    tensor_stats_kernel<<<grid_for((n + 7) / 8, 256, 8), 256, 0, s>>>(x, x_dtype, n, vec, tstat);
+    ::tc::count_launch();
   }
-  if (pl.fused) {
+  if (p.two_level) {
+    tensor_scale_kernel<<<1, 1, 0, s>>>(p, tstat, amax, d2, nullptr, nullptr, nullptr, nullptr, 1);
+    ::tc::count_launch();
+  }
+  if ((st = launch_status("tc_quantize tensor statistic"))) return st;
+  if (pl.path == PATH_GROUP) {
     int L = (int)(p.dc / 4);
     int64_t ngroups = n / p.dc;
-    int64_t threads = ngroups * L;
-    int grid = grid_for(threads, 256, 16);
-#define TC_GROUP_CASE(LL)                                                                                     \
-  case LL:                                                                                                    \
+    int grid = grid_for(ngroups * L, 256, 16);
+#define TC_GROUP_CASE(LL)                                                                                         \
+  case LL:                                                                                                        \
     group_kernel<LL><<<grid, 256, 0, s>>>(x, p, d2, noise, scale_noise, out->values, out->scale, out->zero_point, \
-                                          out->codes, out->scale_codes, out->dequant);                        \
-    ::tc::count_launch();                                                                                     \
+                                          out->codes, out->scale_codes, out->dequant);                            \
+    ::tc::count_launch();                                                                                         \
     break;
     switch (L) {
       TC_GROUP_CASE(1)
@@ -740,21 +945,29 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
     }
 #undef TC_GROUP_CASE
     return launch_status("tc_quantize group pass");
+  }
+  if (pl.path == PATH_ROW) {
+    int grid = (int)(rows < (int64_t)sm_count() * 8 ? rows : (int64_t)sm_count() * 8);
+    row_kernel<<<grid, 256, 0, s>>>(x, p, d2, noise, scale_noise, out->values, out->scale, out->zero_point,
+                                    out->codes, out->scale_codes, out->dequant);
     ::tc::count_launch();
+    return launch_status("tc_quantize row pass");
+  }
+  if (pl.path == PATH_TENSOR) {
+    tensor_scale_kernel<<<1, 1, 0, s>>>(p, tstat, (amax && !p.zp) ? amax : nullptr, d2, scale_noise, out->scale,
+                                        out->zero_point, out->scale_codes, 0);
+    ::tc::count_launch();
+    flat_kernel<<<grid_for((n + 3) / 4, 256, 8), 256, 0, s>>>(x, p, out->scale, out->zero_point, d2, noise,
+                                                             out->values, out->codes, out->dequant);
+    ::tc::count_launch();
+    return launch_status("tc_quantize tensor pass");
   }
   int64_t chunk = cdiv(p.dr * p.dc, pl.parts);
-  if (amax && !p.zp) {  // zero-point ranges always come from the data
-    scale_kernel<<<1, 32, 0, s>>>(p, 1, 0, stats, amax, d2, scale_noise, out->scale, out->zero_point,
-                                  out->scale_codes, 0);
-    ::tc::count_launch();
-  } else {
-    stats_kernel<<<(unsigned)(pl.nd * pl.parts), 256, 0, s>>>(x, p, pl.nd, pl.parts, chunk, stats);
-    ::tc::count_launch();
-    int64_t warps = pl.nd;
-    scale_kernel<<<(unsigned)cdiv(warps * 32, 256), 256, 0, s>>>(p, pl.nd, pl.parts, stats, nullptr, d2, scale_noise,
-                                                                out->scale, out->zero_point, out->scale_codes, 0);
-    ::tc::count_launch();
-  }
+  stats_kernel<<<(unsigned)(pl.nd * pl.parts), 256, 0, s>>>(x, p, pl.nd, pl.parts, chunk, stats);
+  ::tc::count_launch();
+  scale_kernel<<<(unsigned)cdiv(pl.nd * 32, 256), 256, 0, s>>>(p, pl.nd, pl.parts, stats, nullptr, d2, scale_noise,
+                                                              out->scale, out->zero_point, out->scale_codes, 0);
+  ::tc::count_launch();
   if ((st = launch_status("tc_quantize scales"))) return st;
   element_kernel<<<grid_for((n + 1) / 2, 256), 256, 0, s>>>(x, p, out->scale, out->zero_point, d2, noise, out->values,
                                                            out->codes, out->dequant);

@@ -117,8 +117,10 @@ class QuantExtras:
 
 
 def quantize_into(x: torch.Tensor, spec, *, amax=None, noise=None, seed: int = 0, scale_noise=None,
-                  want_codes: bool = False, want_scale_codes: bool = False, want_dequant: bool = False):
-    """Quantize and return ``(QTensor, QuantExtras)``; the extras are written in the same pass."""
+                  want_codes: bool = False, want_scale_codes: bool = False, want_dequant: bool = False,
+                  want_values: bool = True):
+    """Quantize and return ``(QTensor, QuantExtras)``; the extras are written in the same pass.
+    ``want_values=False`` skips the QTensor values (the QTensor then carries ``values=None``)."""
     if x.ndim == 0 or x.numel() == 0:
         raise ValueError("quantization needs a nonempty tensor of shape [..., K]")
     _validate_scale_spec(spec, scale_noise)
@@ -147,7 +149,7 @@ def quantize_into(x: torch.Tensor, spec, *, amax=None, noise=None, seed: int = 0
     sn = None
     if sf is not None and scale_noise is not None:
         sn = _noise(scale_noise, lay, device)
-    values = torch.empty((rows, K), device=device, dtype=container_dtype(spec.format))
+    values = torch.empty((rows, K), device=device, dtype=container_dtype(spec.format)) if want_values else None
     scale = zero = gscale = None
     if sf is not None:
         scale = torch.empty(lay, device=device, dtype=torch.float32)
@@ -167,7 +169,8 @@ def quantize_into(x: torch.Tensor, spec, *, amax=None, noise=None, seed: int = 0
         extras.dequant = torch.empty((rows, K), device=device, dtype=torch.float32)
     qs = _qspec(spec)
     out = N.TcQuantOut()
-    out.values, out.values_dtype = values.data_ptr(), N.dtype_code(values.dtype)
+    out.values = 0 if values is None else values.data_ptr()
+    out.values_dtype = N.dtype_code(container_dtype(spec.format))
     for name, t in (("scale", scale), ("zero_point", zero), ("global_scale", gscale), ("codes", extras.codes),
                     ("scale_codes", extras.scale_codes), ("dequant", extras.dequant)):
         setattr(out, name, 0 if t is None else t.data_ptr())
