@@ -85,6 +85,56 @@ def measure_cfg1(dev, steps: int, warmup: int) -> dict:
             "hbm_peak_gbs": hbm}
 
 
+def measure_gemm_config(dev, name: str, steps: int, warmup: int) -> dict:
+    """Device-resident step of cfg3 (FP8 E4M3 W8A8, Hopper CoFDA F=13 CS=32, 8192^3) or cfg4
+    (INT8 per-token x INT4 g128 asymmetric, CoFDA F=23 promoted every 128, 4096x12288x4096):
+    quantize both operands + emulated GEMM, L2 flushed between steps, CUDA-event timed."""
+    import torch
+
+    from tricast_b200 import as_operand, gemm_triton, quantize_triton
+    from tricast_b200.formats import FP16, IntFormat
+    from tricast_b200.operand import Operand
+    from tricast_b200.spec import PRESETS, SCHEMES, MMASpec
+
+    g = torch.Generator().manual_seed(0)
+    if name == "cfg3":
+        m, n, k = 8192, 8192, 8192
+        a = torch.randn(m, k, generator=g).bfloat16().to(dev)
+        b = (torch.randn(n, k, generator=g) * 0.02).bfloat16().to(dev)
+        spec = PRESETS["nvidia_hopper_fp8"].with_(out_format="fp32")
+
+        def step():
+            qa, qb = quantize_triton(a, SCHEMES["fp8_tensor"]), quantize_triton(b, SCHEMES["fp8_tensor"])
+            return gemm_triton(as_operand(qa), as_operand(qb), spec)
+    else:
+        m, n, k = 4096, 12288, 4096
+        x = torch.randn(m, k, generator=g).to(dev)
+        w = (torch.randn(n, k, generator=g) * 0.02).to(dev)
+        spec = MMASpec("cofda", f_bits=23, chunk_size=32, promote_interval=128, out_format="fp32")
+        int5 = IntFormat("int5", 5)
+
+        def step():
+            qa = quantize_triton(x, SCHEMES["int8_row"])
+            qw = quantize_triton(w, SCHEMES["int4_g128_zp"])
+            bvals = qw.values.float() - qw.zero_point.repeat_interleave(128, dim=1)
+            return gemm_triton(as_operand(qa), Operand(bvals, int5, qw.scale, FP16, "k", 128), spec)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(warmup):
+        step()
+    times = []
+    for _ in range(steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step()
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    t = sum(times) / len(times)
+    return {"workload": name, "shape": [m, n, k], "gmacs": m * n * k / (t * 1e-3) / 1e9, "ms": t}
+
+
 def make_inputs(rank: int):
     """Seeded CPU generation so every GPU count sees identical tensors."""
     import torch
@@ -350,6 +400,7 @@ def run_b200(args) -> None:
         }
         if world == 1:
             line["aux_cast"] = measure_cfg1(dev, args.steps, args.warmup)
+            line["aux_gemm"] = [measure_gemm_config(dev, c, max(2, args.steps // 3), 1) for c in ("cfg3", "cfg4")]
         if world == 1 and not args.no_cpu_baseline:
             v, desc = cpu_oracle_sample(32, 512)
             line["cpu_baseline"] = {"value": v, "unit": "GMAC/s", "cores": 1, "kind": "port", "sample": desc}
@@ -366,13 +417,17 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1"],
-                    help="cfg1 runs only the MXFP4 cast measurement (for profiling)")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1", "cfg3", "cfg4"],
+                    help="cfg1/cfg3/cfg4 run only that measurement (for profiling)")
     args = ap.parse_args()
-    if args.workload == "cfg1" and args.impl != "reference":
+    if args.workload != "cfg2" and args.impl != "reference":
         import torch
 
-        print(json.dumps(measure_cfg1(torch.device("cuda", 0), args.steps, args.warmup)))
+        dev = torch.device("cuda", 0)
+        if args.workload == "cfg1":
+            print(json.dumps(measure_cfg1(dev, args.steps, args.warmup)))
+        else:
+            print(json.dumps(measure_gemm_config(dev, args.workload, args.steps, args.warmup)))
         return
     if args.impl == "reference":
         run_reference(args)

@@ -184,3 +184,23 @@ def test_cofda_chunk8_and_fallback_on_nan():
     a = as_operand(quantize_triton(x.cuda(), SCHEMES["fp8_row"]))
     spec = PRESETS["nvidia_hopper_fp8"].with_(out_format="fp32")
     assert bits_equal(gemm_triton(a, b, spec).cpu().numpy(), _oracle_gemm(a, b, spec))
+
+
+@pytest.mark.parametrize("shape", [(200, 150, 2048), (3, 129, 256)])
+def test_int_promote_fast_path_vs_oracle(shape):
+    """cfg4 mapping (INT8 row x INT5 (uint4 - zero point), F=23 promoted every 128) at larger sizes."""
+    m, n, k = shape
+    g = torch.Generator().manual_seed(40 + m)
+    qa = quantize_triton(torch.randn(m, k, generator=g).cuda(), SCHEMES["int8_row"])
+    qw = quantize_triton((torch.randn(n, k, generator=g) * 0.02).cuda(), SCHEMES["int4_g128_zp"])
+    z = qw.zero_point.repeat_interleave(128, dim=1)[:, :k]
+    a = as_operand(qa)
+    b = Operand(qw.values.float() - z, IntFormat("int5", 5), qw.scale, FP16, "k", 128)
+    spec = MMASpec("cofda", f_bits=23, chunk_size=32, promote_interval=128, out_format="fp32")
+    got = gemm_triton(a, b, spec).cpu().numpy()
+    assert bits_equal(got, _oracle_gemm(a, b, spec))
+    # int_exact on int8 x int8 with row scales (the int8_row_w8a8 recipe's arithmetic)
+    a8 = as_operand(qa)
+    b8 = as_operand(quantize_triton(torch.randn(n, k, generator=g).cuda(), SCHEMES["int8_row"]))
+    spec = MMASpec("int_exact", out_format="fp32")
+    assert bits_equal(gemm_triton(a8, b8, spec).cpu().numpy(), _oracle_gemm(a8, b8, spec))

@@ -423,10 +423,14 @@ static Fp4Plan plan_fp4(const GemmDesc &g) {
 size_t cofda_workspace(const GemmDesc &g);
 int launch_cofda(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
 
+size_t int_workspace(const GemmDesc &g);
+int launch_int(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
+
 size_t fast_workspace(const GemmDesc &g) {
   Fp4Plan p = plan_fp4(g);
   if (p.ok) return p.total;
-  return cofda_workspace(g);
+  size_t w = int_workspace(g);
+  return w ? w : cofda_workspace(g);
 }
 
 template <int NG>
@@ -442,7 +446,10 @@ static int launch_fp4_gemm(const fp4::GemmArgs &args, int64_t M, int64_t N, cuda
 
 int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s) {
   Fp4Plan p = plan_fp4(g);
-  if (!p.ok) return launch_cofda(g, workspace, workspace_bytes, s);
+  if (!p.ok) {
+    int st = launch_int(g, workspace, workspace_bytes, s);
+    return st == TC_UNSUPPORTED ? launch_cofda(g, workspace, workspace_bytes, s) : st;
+  }
   if (!workspace || workspace_bytes < p.total) return set_error("tc_gemm: workspace too small"), TC_WORKSPACE_TOO_SMALL;
   if (p.ntiles * fp4::kTileRows > (int64_t)1 << 40) return TC_UNSUPPORTED;
   char *ws = static_cast<char *>(workspace);
