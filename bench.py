@@ -366,6 +366,13 @@ def run_b200(args) -> None:
     stop.set()
     sampler.join(timeout=5)
 
+    # Layer sweep (cfg5): 196 layers x 4 formats sharded over all ranks, NCCL gather of the metric
+    # sums; a reduced warm-up run first, then the full sweep, device-timed, max over ranks.
+    from tricast_b200.sweep import SweepConfig, run_sweep
+
+    run_sweep(SweepConfig(blocks=1, tokens=256))
+    _, sweep_secs = run_sweep(SweepConfig())
+
     t_step = sum(step_ms) / len(step_ms)
     t_gemm = sum(e0.elapsed_time(e1) for e0, e1 in gemm_events) / len(gemm_events)
     t_e2e = sum(e2e_ms) / len(e2e_ms)
@@ -396,6 +403,10 @@ def run_b200(args) -> None:
                          "note": f"emulated GEMM kernel; peak = 148 SMs x 128 lanes x {sm_mhz:.0f} MHz / "
                                  f"{ops_per_mac:.0f} ops per MAC (two-pass GDFS)"},
             "gemm_ms": t_gemm,
+            "aux_sweep": {"workload": "cfg5 per-layer error sweep: 196 Qwen3-0.6B-shaped layers x "
+                                      "(MXFP4, NVFP4, FP8 E4M3, INT4-g128) vs fp64, 2048 tokens",
+                          "secs": sweep_secs, "n_gpus": world, "sharding": "LPT by layer MACs",
+                          "collective": "NCCL all_gather of [layers, 4, 6] fp64 metric sums"},
             "clocks": clk,
         }
         if world == 1:

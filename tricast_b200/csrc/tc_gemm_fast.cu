@@ -424,6 +424,7 @@ size_t cofda_workspace(const GemmDesc &g);
 int launch_cofda(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
 
 size_t int_workspace(const GemmDesc &g);
+int launch_fma(const GemmDesc &g, cudaStream_t s);
 int launch_int(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
 
 size_t fast_workspace(const GemmDesc &g) {
@@ -448,7 +449,10 @@ int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
   Fp4Plan p = plan_fp4(g);
   if (!p.ok) {
     int st = launch_int(g, workspace, workspace_bytes, s);
-    return st == TC_UNSUPPORTED ? launch_cofda(g, workspace, workspace_bytes, s) : st;
+    if (st != TC_UNSUPPORTED) return st;
+    st = launch_cofda(g, workspace, workspace_bytes, s);
+    if (st != TC_UNSUPPORTED) return st;
+    return launch_fma(g, s);
   }
   if (!workspace || workspace_bytes < p.total) return set_error("tc_gemm: workspace too small"), TC_WORKSPACE_TOO_SMALL;
   if (p.ntiles * fp4::kTileRows > (int64_t)1 << 40) return TC_UNSUPPORTED;
