@@ -52,19 +52,22 @@ def make_cfg1_input():
 
 def measure_cfg1(dev, steps: int, warmup: int) -> dict:
     """MXFP4 quantize-dequantize cast of cfg1 with BASELINE's outputs (dequant fp32, packed E2M1
-    codes, E8M0 scale bytes); inputs resident, L2 flushed between launches, CUDA-event timed."""
+    codes, E8M0 scale bytes); inputs resident, outputs preallocated (QuantizePlan), L2 flushed
+    between launches, CUDA-event timed."""
     import torch
 
-    from tricast_b200 import quantize_into
+    from tricast_b200 import QuantizePlan
     from tricast_b200.spec import SCHEMES
 
     x = make_cfg1_input().to(dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     spec = SCHEMES["mxfp4"]
     stream = torch.cuda.current_stream(dev)
+    plan = QuantizePlan(x.shape, x.dtype, dev, spec, want_values=False, want_codes=True, want_scale_codes=True,
+                        want_dequant=True)
 
     def run():
-        return quantize_into(x, spec, want_values=False, want_codes=True, want_scale_codes=True, want_dequant=True)
+        return plan.run(x)
 
     for _ in range(warmup):
         run()
@@ -78,11 +81,26 @@ def measure_cfg1(dev, steps: int, warmup: int) -> dict:
         e1.synchronize()
         times.append(e0.elapsed_time(e1))
     t = sum(times) / len(times)
+    # The same protocol around a plain device copy of x (4 + 4 bytes per element): the practical
+    # ceiling of a short streaming kernel, reported beside the STREAM-measured peak.
+    y = torch.empty_like(x)
+    copy_times = []
+    for i in range(warmup + steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        y.copy_(x)
+        e1.record(stream)
+        e1.synchronize()
+        if i >= warmup:
+            copy_times.append(e0.elapsed_time(e1))
+    tc = sum(copy_times) / len(copy_times)
     gbs = x.numel() * CFG1_BYTES_PER_ELEM / (t * 1e-3) / 1e9
     hbm = measured_peaks().get("hbm_gbs", 6650.0)
     return {"workload": "cfg1 MXFP4 quantize-dequantize 4096x4096 fp32 (dequant fp32 + packed E2M1 + E8M0 bytes)",
             "gbs": gbs, "ms": t, "bytes_per_elem": CFG1_BYTES_PER_ELEM, "hbm_frac": gbs / hbm,
-            "hbm_peak_gbs": hbm}
+            "hbm_peak_gbs": hbm, "copy_same_protocol_gbs": x.numel() * 8 / (tc * 1e-3) / 1e9,
+            "copy_same_protocol_ms": tc}
 
 
 def measure_gemm_config(dev, name: str, steps: int, warmup: int) -> dict:

@@ -18,7 +18,7 @@ from . import formats, rounding, spec  # noqa: F401
 from .formats import get_format  # noqa: F401
 from .mma import gemm, gemm_triton  # noqa: F401
 from .operand import Operand, QTensor, as_operand  # noqa: F401
-from .quantize import quantize, quantize_into, quantize_triton, round_to_format_triton  # noqa: F401
+from .quantize import QuantizePlan, quantize, quantize_into, quantize_triton, round_to_format_triton  # noqa: F401
 from .spec import PRESETS, SCHEMES, MMASpec, QuantSpec, ScaleSpec, get_preset, get_scheme  # noqa: F401
 
 __version__ = "0.1.0"

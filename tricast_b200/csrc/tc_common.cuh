@@ -11,7 +11,7 @@
 
 #include <string>
 
-#include "../../include/tricast_b200.h"
+#include "tricast_b200.h"
 
 namespace tc {
 

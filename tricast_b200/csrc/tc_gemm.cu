@@ -139,8 +139,11 @@ __device__ __forceinline__ Term gdfs_group(const GemmDesc &g, int64_t m, int64_t
   return r;
 }
 
+// only_if_flag, when given, points at the fast path's {fallback flag, timeout status} pair: the
+// exact kernel runs behind a fast kernel only if the fast kernel declined the operands or one of its
+// bounded waits gave up, so a timeout still ends in the exact result.
 __global__ void __launch_bounds__(256) gemm_generic_kernel(GemmDesc g, const int32_t *only_if_flag) {
-  if (only_if_flag && *only_if_flag == 0) return;  // behind a fast kernel that took the product
+  if (only_if_flag && only_if_flag[0] == 0 && only_if_flag[1] == 0) return;  // the fast kernel took it
   int64_t n = (int64_t)blockIdx.x * 16 + (threadIdx.x & 15);
   int64_t m = (int64_t)blockIdx.y * 16 + (threadIdx.x >> 4);
   if (m >= g.M || n >= g.N) return;

@@ -1,241 +1,26 @@
 // Cast and quantize kernels (TriCast round_to_format / quantize, src/tricast/reference/cast.py and
-// src/tricast/reference/quantize.py).
+// src/tricast/reference/quantize.py), and the host dispatch of tc_cast / tc_quantize.
 //
-// Quantize runs one of two pipelines:
-//  * fused group pass — granularity "group" with group_size in {4,...,128} dividing K: each group is
+// Quantize runs one of these pipelines:
+//  * lean group pass (tc_quant_lean.cuh) — granularity "group" with a float element format, absmax or
+//    power-of-two scale, nearest-even or directed rounding, no zero point: one pass over x with 16
+//    elements per lane (8 for groups of 8), the next iteration's loads in flight while the current
+//    one computes; the last few groups take the four-elements-per-lane pass below;
+//  * fused group pass — any other group spec with group_size in {4,...,128} dividing K: each group is
 //    owned by group_size/4 adjacent lanes that load 4 elements each with one vector load, reduce the
 //    domain statistic with warp shuffles, compute the scale, and write values / scale / codes /
 //    dequant in the same pass, so x is read from HBM once;
-//  * general pass — any granularity: (A) per-domain partial statistics, (B) one warp per domain
-//    combines partials and derives scale and zero point, (C) element rounding.
+//  * row pass, tensor pass (statistic kernel + element kernel) and the general pass — any
+//    granularity: (A) per-domain partial statistics, (B) one warp per domain combines partials and
+//    derives scale and zero point, (C) element rounding.
 // Two-level specs first reduce the tensor amax and derive the global decode scale d2 on the device.
-#include <cmath>
-#include <cstring>
-#include <string>
+// The direct cast and the tensor pass use the lean cast (tc_lean.cuh) where the format allows.
+#include <algorithm>
 
-#include "tc_common.cuh"
+#include "tc_quant.cuh"
+#include "tc_quant_lean.cuh"
 
 namespace tc {
-
-enum { GRAN_TENSOR = 0, GRAN_ROW = 1, GRAN_GROUP = 2, GRAN_BLOCK = 3 };
-enum { M_ABSMAX = 0, M_POW2_FLOOR = 1, M_POW2_CEIL = 2, M_MSE = 3, M_PERCENTILE = 4 };
-enum { ZP_NONE = 0, ZP_INT = 1, ZP_FLOAT = 2 };
-
-struct QParams {
-  Fmt ef, sf;
-  int64_t rows, K;
-  int64_t dr, dc, nr, nc;  // nominal domain rect and domain grid
-  int has_scale, method, srnd, two_level, zp, rnd, sr_bits, saturate;
-  float max_elem;          // element max_normal (exact in fp32)
-  double max_elem_d;
-  int emax_elem;
-  uint32_t min_scale_bits;  // scale format min_subnormal (pow2: min_normal) as fp32
-  double qmin_d, qmax_d;
-  float qrange;             // qmax - qmin
-  int x_dtype, v_dtype;
-  int code_bits;            // 0, 4 or 8
-  int scode;                // 0 none, 1 byte code of the scale format
-  double prod_max_d;        // element max * scale max (two-level global scale)
-  int pow2_div;             // every divisor is a power of two (pow2 methods, one level)
-};
-
-// ------------------------------------------------------------------ element codes
-// Bit encoding of a grid value in a <= 8-bit format (sign | exponent field | fraction field, or
-// two's complement k for integers). NaN uses the format's NaN encoding where it has one.
-__device__ __forceinline__ uint32_t element_code(float v, const Fmt &f, int total_bits) {
-  uint32_t u = f2u(v);
-  uint32_t sign = u >> 31;
-  uint32_t a = u & 0x7FFFFFFFu;
-  if (f.kind == 1) {
-    if (a > kInf) return 0u;
-    double k = ldexp((double)fabsf(v), f.frac_bits);
-    int64_t ki = (int64_t)k;
-    if (sign && a) ki = -ki;
-    return (uint32_t)ki & ((1u << total_bits) - 1u);
-  }
-  int mb = f.mbits;
-  uint32_t mmask = (1u << mb) - 1u;
-  uint32_t top_field = (1u << f.ebits) - 1u;
-  uint32_t code;
-  if (a > kInf) {
-    if (f.special == 1) code = (top_field << mb) | mmask;                // fn: all ones
-    else if (f.special == 2) return 1u << (total_bits - 1);              // fnuz: the "-0" pattern
-    else if (f.special == 0) code = (top_field << mb) | (mb ? (1u << (mb - 1)) : 0u);
-    else code = 0u;
-    sign = 0;
-  } else if (a == kInf) {
-    code = top_field << mb;
-  } else if (a == 0) {
-    code = 0u;
-  } else {
-    int field = (int)(a >> 23);
-    int e32 = field ? field - 127 : -126;
-    uint32_t sig = field ? ((a & 0x7FFFFFu) | 0x800000u) : a;
-    if (e32 >= f.emin) {
-      code = ((uint32_t)(e32 + f.bias) << mb) | ((sig >> (23 - mb)) & mmask);
-    } else {
-      int s = 23 - mb + (f.emin - e32);   // fraction of a subnormal in units of 2**(emin - mbits)
-      code = s >= 32 ? 0u : (sig >> s);
-    }
-  }
-  if (f.is_signed) code |= sign << (f.ebits + mb);
-  return code & ((1u << total_bits) - 1u);
-}
-
-__device__ __forceinline__ uint32_t scale_code(float s, const Fmt &f) {
-  if (f.kind == 2) {
-    uint32_t a = f2u(s);
-    if ((a & 0x7FFFFFFFu) > kInf) return 0xFFu;
-    int e;
-    frexpf(s, &e);
-    return (uint32_t)(e - 1 + f.bias) & 0xFFu;
-  }
-  return element_code(s, f, f.ebits + f.mbits + (f.is_signed ? 1 : 0));
-}
-
-// ------------------------------------------------------------------ scale selection
-__device__ __forceinline__ float amax_scale(float amax, float d2, bool has_d2, const QParams &p, uint32_t noise) {
-  float t = __fdiv_rn(amax, p.max_elem);
-  if (has_d2) t = __fdiv_rn(t, d2);
-  float s = cast_to(t, p.sf, p.srnd, true, noise, 32);
-  if (s == 0.0f) s = u2f(p.min_scale_bits);
-  if (amax == 0.0f) s = 1.0f;
-  return s;
-}
-
-__device__ __forceinline__ float pow2_scale(float amax, const QParams &p) {
-  double a = amax == 0.0f ? ldexp(1.0, -126) : (double)amax;
-  int ex;
-  frexp(a, &ex);
-  int e = ex - 1 - p.emax_elem;
-  if (p.method == M_POW2_CEIL && ldexp(p.max_elem_d, e) < a) e += 1;
-  bool overflow = e > p.sf.emax || !isfinite(a);
-  e = e < p.sf.emin ? p.sf.emin : (e > p.sf.emax ? p.sf.emax : e);
-  float s = __double2float_rn(ldexp(1.0, e));
-  return overflow ? u2f(kQNaN) : s;
-}
-
-// One exact binary32 rounding of amax / P, P = element max * scale max, as TriCast's
-// _global_scale (src/tricast/reference/quantize.py:195-219): the fp64 quotient gives a candidate
-// and the midpoints to its neighbours are tested exactly with fma (the sign of m*P - amax).
-__device__ float global_scale(float amax, double P) {
-  if (!isfinite(amax)) return amax;
-  if (amax == 0.0f) return 1.0f;
-  double A = (double)amax;
-  float r = __double2float_rn(A / P);
-  for (int it = 0; it < 2; ++it) {
-    float up = nextafterf(r, INFINITY);
-    double mid = 0.5 * ((double)r + (double)up);
-    double s = fma(mid, P, -A);
-    if (s < 0 || (s == 0 && (f2u(r) & 1u))) r = up;
-    float dn = nextafterf(r, -INFINITY);
-    mid = 0.5 * ((double)r + (double)dn);
-    s = fma(mid, P, -A);
-    if (s > 0 || (s == 0 && (f2u(r) & 1u))) r = dn;
-  }
-  return r == 0.0f ? 1.0f : r;
-}
-
-// Affine scale and zero point from the domain range (src/tricast/reference/quantize.py:176-192).
-__device__ __forceinline__ void zp_scale(float lo, float hi, const QParams &p, uint32_t noise, float &s, float &z) {
-  if (p.zp == ZP_INT) {
-    if (lo > 0.0f) lo = 0.0f;  // clamp(max=0): keeps -0 and NaN
-    if (hi < 0.0f) hi = 0.0f;
-  }
-  float raw = __fdiv_rn(__fsub_rn(hi, lo), p.qrange);
-  s = cast_to(raw, p.sf, p.srnd, true, noise, 32);
-  if (s == 0.0f) s = u2f(p.min_scale_bits);
-  if (hi == lo) s = 1.0f;
-  z = lo;
-  if (p.zp == ZP_INT) {
-    float t = rintf(__fsub_rn((float)p.qmin_d, __fdiv_rn(lo, s)));
-    if (t < (float)p.qmin_d) t = (float)p.qmin_d;
-    if (t > (float)p.qmax_d) t = (float)p.qmax_d;
-    z = t;  // NaN stays NaN (both comparisons false)
-  }
-}
-
-// Order-preserving keys: -0 sorts below +0.
-__device__ __forceinline__ uint32_t fkey(float v) {
-  uint32_t u = f2u(v);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ float unkey(uint32_t k) { return u2f((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k); }
-
-// ------------------------------------------------------------------ element rounding
-// Integer rounding for zero-point specs on the unbounded integer grid, then + z and clamp
-// (src/tricast/reference/quantize.py:325-332).
-__device__ __forceinline__ float zp_round(float xq, float z, const QParams &p, uint32_t noise) {
-  uint32_t u = f2u(xq);
-  uint32_t a = u & 0x7FFFFFFFu;
-  double r;
-  if (a > kInf) {
-    r = (double)xq;
-  } else if (a == kInf) {
-    r = (double)xq;
-  } else {
-    bool neg = (u >> 31) && a;
-    uint32_t field = a >> 23;
-    uint32_t sig = field ? ((a & 0x7FFFFFu) | 0x800000u) : a;
-    int e32 = field ? (int)field - 127 : -126;
-    int shift = 23 - e32;  // quantum 2**0
-    double k;
-    if (shift <= 0) {
-      k = (double)fabsf(xq);
-    } else {
-      uint32_t kept = shift >= 32 ? 0u : (sig >> shift);
-      uint32_t rem = shift >= 32 ? sig : (sig & ((1u << shift) - 1u));
-      kept += round_inc(kept, rem, shift, neg, p.rnd, noise, p.sr_bits) ? 1u : 0u;
-      k = (double)kept;
-    }
-    r = (u >> 31) ? -k : k;
-  }
-  if (p.zp == ZP_INT) r = r + (double)z;
-  if (r < p.qmin_d) r = p.qmin_d;
-  if (r > p.qmax_d) r = p.qmax_d;
-  return (float)r;
-}
-
-struct ElemOut {
-  float value;
-  float dequant;
-};
-
-// The divisor of a domain: s (one level) or RN(s * d2) (two-level), and, when it is a power of two,
-// its exact reciprocal: RN(x / 2**e) == RN(x * 2**-e) for every fp32 x, 2**-e being representable.
-struct Divisor {
-  float eff, inv;
-  bool by_inv;
-};
-
-__device__ __forceinline__ Divisor make_divisor(float s, float d2, bool has_d2, const QParams &p) {
-  Divisor d;
-  d.eff = has_d2 ? __fmul_rn(s, d2) : s;
-  d.by_inv = p.pow2_div != 0;
-  d.inv = d.by_inv ? __frcp_rn(d.eff) : 0.0f;
-  return d;
-}
-
-__device__ __forceinline__ ElemOut quant_elem_d(float x, float s, float z, const Divisor &dv, float d2, bool has_d2,
-                                                const QParams &p, uint32_t noise) {
-  float xq = x;
-  if (p.zp == ZP_FLOAT) xq = __fsub_rn(xq, z);
-  if (p.has_scale) xq = dv.by_inv ? __fmul_rn(xq, dv.inv) : __fdiv_rn(xq, dv.eff);
-  ElemOut o;
-  o.value = p.zp ? zp_round(xq, z, p, noise) : cast_to(xq, p.ef, p.rnd, p.saturate, noise, p.sr_bits);
-  float d = o.value;
-  if (p.zp == ZP_INT) d = __fsub_rn(d, z);
-  if (p.has_scale) d = __fmul_rn(d, s);
-  if (p.zp == ZP_FLOAT) d = __fadd_rn(d, z);
-  if (has_d2) d = __fmul_rn(d, d2);
-  o.dequant = d;
-  return o;
-}
-
-__device__ __forceinline__ ElemOut quant_elem(float x, float s, float z, float d2, bool has_d2, const QParams &p,
-                                              uint32_t noise) {
-  return quant_elem_d(x, s, z, make_divisor(s, d2, has_d2, p), d2, has_d2, p, noise);
-}
 
 // ------------------------------------------------------------------ cast kernel
 __global__ void __launch_bounds__(256) cast_kernel(const float *__restrict__ x, float *__restrict__ y,
@@ -260,6 +45,34 @@ __global__ void __launch_bounds__(256) cast_kernel(const float *__restrict__ x, 
   } else {
     for (int64_t i = tid; i < n; i += stride) y[i] = cast_to(x[i], f, rnd, saturate, noise ? noise[i] : 0u, sr_bits);
   }
+}
+
+// Lean cast of one value of any class: NaN passes through, Inf and huge magnitudes overflow.
+template <int RND>
+__device__ __forceinline__ float lean_cast(float v, const Lean &l) {
+  const uint32_t u = f2u(v);
+  const uint32_t sign = u & 0x80000000u;
+  const float r = lean_overflow(lean_mag<RND, true>(v, l), sign, l);
+  return (u & 0x7FFFFFFFu) > kInf ? v : u2f(f2u(r) | sign);
+}
+
+// round_to_format for the lean-eligible formats and roundings, 8 elements per thread.
+template <int RND>
+__global__ void __launch_bounds__(256) cast_lean_kernel(const float *__restrict__ x, float *__restrict__ y, int64_t n,
+                                                        Lean l) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t n8 = n >> 3;
+  for (int64_t i = tid; i < n8; i += stride) {
+    const float4 *src = reinterpret_cast<const float4 *>(x) + 2 * i;
+    float4 a = src[0], b = src[1];
+    a.x = lean_cast<RND>(a.x, l); a.y = lean_cast<RND>(a.y, l); a.z = lean_cast<RND>(a.z, l); a.w = lean_cast<RND>(a.w, l);
+    b.x = lean_cast<RND>(b.x, l); b.y = lean_cast<RND>(b.y, l); b.z = lean_cast<RND>(b.z, l); b.w = lean_cast<RND>(b.w, l);
+    float4 *dst = reinterpret_cast<float4 *>(y) + 2 * i;
+    dst[0] = a;
+    dst[1] = b;
+  }
+  for (int64_t i = (n8 << 3) + tid; i < n; i += stride) y[i] = lean_cast<RND>(x[i], l);
 }
 
 static int sm_count() {
@@ -685,7 +498,9 @@ __global__ void tensor_scale_kernel(QParams p, const Stat *__restrict__ st, cons
 }
 
 // Elements of a single-domain (tensor) spec, or of a direct cast: 4 consecutive elements per thread.
-__global__ void __launch_bounds__(256) flat_kernel(const void *__restrict__ x, QParams p,
+// RND >= 0 selects the lean cast for that rounding (float formats, no zero point, no noise).
+template <int RND>
+__global__ void __launch_bounds__(256) flat_kernel(const void *__restrict__ x, QParams p, Lean ln,
                                                    const float *__restrict__ scale, const float *__restrict__ zero,
                                                    const float *__restrict__ d2p, const uint32_t *__restrict__ noise,
                                                    void *__restrict__ values, uint8_t *__restrict__ codes,
@@ -708,11 +523,28 @@ __global__ void __launch_bounds__(256) flat_kernel(const void *__restrict__ x, Q
     }
     float o[4], dq[4];
     uint32_t cd[4] = {0, 0, 0, 0};
+#pragma unroll
     for (int j = 0; j < 4; ++j) {
-      ElemOut e = quant_elem_d(v[j], sc, z, dv, d2, p.two_level, p, noise && i0 + j < n ? noise[i0 + j] : 0u);
-      o[j] = e.value;
-      dq[j] = e.dequant;
-      if (codes) cd[j] = element_code(e.value, p.ef, p.code_bits == 4 ? 4 : 8);
+      if (RND >= 0) {
+        float xq = v[j];
+        if (p.has_scale) xq = dv.by_inv ? __fmul_rn(xq, dv.inv) : __fdiv_rn(xq, dv.eff);
+        const float val = lean_cast<RND < 0 ? 0 : RND>(xq, ln);
+        float d = val;
+        if (p.has_scale) d = __fmul_rn(d, sc);
+        if (p.two_level) d = __fmul_rn(d, d2);
+        o[j] = val;
+        dq[j] = d;
+        if (codes) {
+          const float mag = fabsf(val);
+          cd[j] = mag <= ln.maxv ? lean_code(mag, ln) | ((f2u(val) >> 31) << ln.sign_pos)
+                                 : element_code(val, p.ef, p.code_bits == 4 ? 4 : 8);
+        }
+      } else {
+        ElemOut e = quant_elem_d(v[j], sc, z, dv, d2, p.two_level, p, noise && i0 + j < n ? noise[i0 + j] : 0u);
+        o[j] = e.value;
+        dq[j] = e.dequant;
+        if (codes) cd[j] = element_code(e.value, p.ef, p.code_bits == 4 ? 4 : 8);
+      }
     }
     for (int j = 0; j < 4 && i0 + j < n; ++j) {
       if (values) store_container(values, p.v_dtype, i0 + j, o[j]);
@@ -726,6 +558,18 @@ __global__ void __launch_bounds__(256) flat_kernel(const void *__restrict__ x, Q
   }
 }
 
+static void launch_flat(int grid, cudaStream_t s, const void *x, const QParams &p, const Lean &ln, int lean_rnd,
+                        const float *scale, const float *zero, const float *d2, const uint32_t *noise, void *values,
+                        uint8_t *codes, float *dequant) {
+  switch (lean_rnd) {
+    case TC_RNE: flat_kernel<TC_RNE><<<grid, 256, 0, s>>>(x, p, ln, scale, zero, d2, noise, values, codes, dequant); break;
+    case TC_RTZ: flat_kernel<TC_RTZ><<<grid, 256, 0, s>>>(x, p, ln, scale, zero, d2, noise, values, codes, dequant); break;
+    case TC_RUP: flat_kernel<TC_RUP><<<grid, 256, 0, s>>>(x, p, ln, scale, zero, d2, noise, values, codes, dequant); break;
+    case TC_RDN: flat_kernel<TC_RDN><<<grid, 256, 0, s>>>(x, p, ln, scale, zero, d2, noise, values, codes, dequant); break;
+    default: flat_kernel<-1><<<grid, 256, 0, s>>>(x, p, ln, scale, zero, d2, noise, values, codes, dequant); break;
+  }
+}
+
 // ------------------------------------------------------------------ host side
 static int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
@@ -735,10 +579,12 @@ static int stats_parts(int64_t domain_elems) {
   return (int)(parts < 1 ? 1 : parts);
 }
 
-enum { PATH_FLAT = 0, PATH_GROUP = 1, PATH_ROW = 2, PATH_TENSOR = 3, PATH_GENERAL = 4 };
+enum { PATH_FLAT = 0, PATH_GROUP = 1, PATH_ROW = 2, PATH_TENSOR = 3, PATH_GENERAL = 4, PATH_GROUP_LEAN = 5 };
 
 struct Plan {
   QParams p;
+  Lean ln;
+  LeanPow2 lp;
   int64_t nd;
   int parts;          // per-domain partials of the general path
   int path;
@@ -757,6 +603,7 @@ static int make_plan(const void *x, int32_t x_dtype, int64_t rows, int64_t K, co
   if (x_dtype < 0 || x_dtype > 2) return set_error("unsupported input dtype"), TC_INVALID_ARGUMENT;
   if (spec->sr_bits < 1 || spec->sr_bits > 32) return set_error("sr_bits must be in [1, 32]"), TC_INVALID_ARGUMENT;
   p.ef = derive(spec->format);
+  pl.ln = make_lean(spec->format, p.ef, spec->rounding, spec->saturate);
   p.rows = rows;
   p.K = K;
   p.has_scale = spec->has_scale;
@@ -839,13 +686,32 @@ static int make_plan(const void *x, int32_t x_dtype, int64_t rows, int64_t K, co
                   (!out->values || ((uintptr_t)out->values % 16) == 0) &&
                   (!out->dequant || ((uintptr_t)out->dequant % 16) == 0) &&
                   (!out->codes || ((uintptr_t)out->codes % 4) == 0);
-  if (group_ok) pl.path = PATH_GROUP;
+  // The lean group pass: float elements with a nearest-even or directed rounding, no zero point,
+  // 8 elements per lane (group sizes 8..128), absmax or power-of-two scales.
+  const bool pow2_method = !p.two_level && (p.method == M_POW2_FLOOR || p.method == M_POW2_CEIL);
+  bool lean_ok = group_ok && pl.ln.ok && !p.zp && gs % 8 == 0 && (p.two_level || p.method == M_ABSMAX || pow2_method) &&
+                 (!out->codes || ((uintptr_t)out->codes % (p.code_bits == 4 ? 8 : 16)) == 0);
+  if (pow2_method) {
+    float mx = (float)p.max_elem_d;
+    uint32_t mb;
+    std::memcpy(&mb, &mx, 4);
+    pl.lp.max_sig = (mb & 0x7FFFFFu) | 0x800000u;
+    pl.lp.emax_elem = p.emax_elem;
+    pl.lp.emin = p.sf.emin;
+    pl.lp.emax = p.sf.emax;
+    pl.lp.bias = p.sf.bias;
+    pl.lp.e8m0_code = spec->scale_format.kind == 2;
+    lean_ok = lean_ok && (spec->scale_format.kind == 2 || spec->scale_format.kind == 0) && p.sf.emin >= -127 &&
+              p.sf.emax <= 127 && (mb >> 23) != 0;
+  }
+  if (lean_ok) pl.path = PATH_GROUP_LEAN;
+  else if (group_ok) pl.path = PATH_GROUP;
   else if (p.dr == 1 && p.dc == K && (!out->codes || p.code_bits == 8 || K % 2 == 0)) pl.path = PATH_ROW;
   else if (p.nr == 1 && p.nc == 1) pl.path = PATH_TENSOR;
   else pl.path = PATH_GENERAL;
   pl.parts = stats_parts(p.dr * p.dc);
   pl.ws_stats = pl.path == PATH_GENERAL ? sizeof(Stat) * (size_t)pl.nd * pl.parts : 0;
-  pl.total = ((pl.ws_stats + 255) & ~(size_t)255) + 256;
+  pl.total = ((pl.ws_stats + 255) & ~(size_t)255) + 256;  // + tensor Stat slot
   return TC_OK;
 }
 
@@ -864,6 +730,19 @@ extern "C" int tc_cast(const float *x, float *y, const uint32_t *noise, int64_t 
   if (sr_bits < 1 || sr_bits > 32) return set_error("sr_bits must be in [1, 32]"), TC_INVALID_ARGUMENT;
   if (n <= 0) return TC_OK;
   Fmt f = derive(*fmt);
+  const Lean ln = make_lean(*fmt, f, rounding, saturate);
+  if (ln.ok && (uintptr_t)x % 16 == 0 && (uintptr_t)y % 16 == 0) {
+    const int grid = grid_for((n + 7) / 8, 256);
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (rounding) {
+      case TC_RNE: cast_lean_kernel<TC_RNE><<<grid, 256, 0, s>>>(x, y, n, ln); break;
+      case TC_RTZ: cast_lean_kernel<TC_RTZ><<<grid, 256, 0, s>>>(x, y, n, ln); break;
+      case TC_RUP: cast_lean_kernel<TC_RUP><<<grid, 256, 0, s>>>(x, y, n, ln); break;
+      default: cast_lean_kernel<TC_RDN><<<grid, 256, 0, s>>>(x, y, n, ln); break;
+    }
+    ::tc::count_launch();
+    return launch_status("tc_cast");
+  }
   int vec = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (!noise || (uintptr_t)noise % 16 == 0);
   cast_kernel<<<grid_for(vec ? (n + 3) / 4 : n, 256), 256, 0, (cudaStream_t)stream>>>(x, y, noise, n, f, rounding,
                                                                                    saturate, sr_bits, vec);
@@ -905,10 +784,11 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
   Stat *tstat = reinterpret_cast<Stat *>(ws + ((pl.ws_stats + 255) & ~(size_t)255));
   float *d2 = out->global_scale;
   const int64_t n = rows * K;
+  const int lean_rnd = (pl.ln.ok && !p.zp && !noise) ? spec->rounding : -1;
   const int vec = ((uintptr_t)x % 16) == 0;
   if (pl.path == PATH_FLAT) {
-    flat_kernel<<<grid_for((n + 3) / 4, 256, 8), 256, 0, s>>>(x, p, nullptr, nullptr, nullptr, noise, out->values,
-                                                             out->codes, out->dequant);
+    launch_flat(grid_for((n + 3) / 4, 256, 8), s, x, p, pl.ln, lean_rnd, nullptr, nullptr, nullptr, noise,
+                out->values, out->codes, out->dequant);
     ::tc::count_launch();
     return launch_status("tc_quantize elements");
   }
@@ -925,6 +805,83 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
     ::tc::count_launch();
   }
   if ((st = launch_status("tc_quantize tensor statistic"))) return st;
+  if (pl.path == PATH_GROUP_LEAN) {
+    const int gs = (int)p.dc;
+    const bool pow2 = !p.two_level && p.method != M_ABSMAX;
+    const bool fast = spec->rounding == TC_RNE && pl.ln.sat_only;
+    const int outs = (!out->values && out->dequant) ? 1 : (out->values && !out->dequant && p.v_dtype == TC_BF16) ? 2 : 0;
+    LeanArgs la;
+    std::memset(&la, 0, sizeof(la));
+    la.x = x;
+    la.p = p;
+    la.ln = pl.ln;
+    la.lp = pl.lp;
+    la.cm.hi = 1u << (32 - pl.ln.mshift);
+    la.cm.two = 2u;
+    la.cm.neg_k = 0u - ((1u << (31 - pl.ln.mshift)) - (1u << pl.ln.sign_pos));
+    la.cm.radix = p.code_bits == 4 ? 16u : 256u;
+    la.d2 = d2;
+    la.scale_noise = scale_noise;
+    la.values = out->values;
+    la.scale = out->scale;
+    la.codes = out->codes;
+    la.scodes = out->scale_codes;
+    la.dequant = out->dequant;
+    // The register-staged kernel over whole warp iterations, then the four-elements-per-lane pass
+    // over the last few groups (pointers offset to that range).
+    int64_t done = 0;
+    {
+      const int esz = x_dtype == TC_F32 ? 4 : 2;
+      const int vsz = out->values_dtype == TC_F32 ? 4 : 2;
+      auto shifted = [&](int64_t off, int64_t count) {
+        LeanArgs r = la;
+        r.p.rows = 1;
+        r.p.K = count;
+        r.x = static_cast<const char *>(x) + off * esz;
+        r.values = out->values ? static_cast<char *>(out->values) + off * vsz : nullptr;
+        r.codes = out->codes ? out->codes + (p.code_bits == 4 ? off / 2 : off) : nullptr;
+        r.scodes = out->scale_codes ? out->scale_codes + off / gs : nullptr;
+        r.dequant = out->dequant ? out->dequant + off : nullptr;
+        r.scale = out->scale + off / gs;
+        r.scale_noise = scale_noise ? scale_noise + off / gs : nullptr;
+        return r;
+      };
+      const int64_t rest_groups = (n - done) / gs;
+      const int lanes_per_group = gs == 8 ? 1 : gs / 16;  // 8 elements per lane for gs 8, else 16
+      const int64_t per_warp = 32 / lanes_per_group;
+      const int64_t main_groups = rest_groups / per_warp * per_warp;
+      if (main_groups > 0) {
+        const LeanArgs r = shifted(done, main_groups * gs);
+        const int grid = grid_for(main_groups * lanes_per_group, 256, 8);
+        const int gi = gs == 8 ? 0 : gs == 16 ? 1 : gs == 32 ? 2 : gs == 64 ? 3 : 4;
+        if (!out->codes) launch_group_lean_c0(r, grid, gi, pow2, fast, outs, s);
+        else if (p.code_bits == 4) launch_group_lean_c4(r, grid, gi, pow2, fast, outs, s);
+        else launch_group_lean_c8(r, grid, gi, pow2, fast, outs, s);
+        ::tc::count_launch();
+        done += main_groups * gs;
+      }
+      if (done < n) {
+        const LeanArgs r = shifted(done, n - done);
+        const int L = gs / 4;
+        const int tgrid = grid_for((n - done) / gs * L, 256, 16);
+#define TC_TAIL_CASE(LL)                                                                                   \
+  case LL:                                                                                                 \
+    group_kernel<LL><<<tgrid, 256, 0, s>>>(r.x, r.p, d2, nullptr, r.scale_noise, r.values, r.scale, nullptr, \
+                                           r.codes, r.scodes, r.dequant);                                  \
+    break;
+        switch (L) {
+          TC_TAIL_CASE(2)
+          TC_TAIL_CASE(4)
+          TC_TAIL_CASE(8)
+          TC_TAIL_CASE(16)
+          TC_TAIL_CASE(32)
+        }
+#undef TC_TAIL_CASE
+        ::tc::count_launch();
+      }
+    }
+    return launch_status("tc_quantize lean group pass");
+  }
   if (pl.path == PATH_GROUP) {
     int L = (int)(p.dc / 4);
     int64_t ngroups = n / p.dc;
@@ -957,8 +914,8 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
     tensor_scale_kernel<<<1, 1, 0, s>>>(p, tstat, (amax && !p.zp) ? amax : nullptr, d2, scale_noise, out->scale,
                                         out->zero_point, out->scale_codes, 0);
     ::tc::count_launch();
-    flat_kernel<<<grid_for((n + 3) / 4, 256, 8), 256, 0, s>>>(x, p, out->scale, out->zero_point, d2, noise,
-                                                             out->values, out->codes, out->dequant);
+    launch_flat(grid_for((n + 3) / 4, 256, 8), s, x, p, pl.ln, lean_rnd, out->scale, out->zero_point, d2, noise,
+                out->values, out->codes, out->dequant);
     ::tc::count_launch();
     return launch_status("tc_quantize tensor pass");
   }

@@ -184,6 +184,49 @@ def quantize_into(x: torch.Tensor, spec, *, amax=None, noise=None, seed: int = 0
     return cls(values, scale, zero, gscale, spec, shape), extras
 
 
+class QuantizePlan:
+    """A quantize call prepared once for a fixed input shape, dtype and spec: outputs, workspace and
+    the C descriptors are allocated up front, so ``run(x)`` is one library call that overwrites them
+    (for loops that quantize same-shaped tensors repeatedly). Deterministic roundings only."""
+
+    def __init__(self, shape, dtype: torch.dtype, device, spec, *, want_values: bool = True,
+                 want_codes: bool = False, want_scale_codes: bool = False, want_dequant: bool = False):
+        _validate_scale_spec(spec, None)
+        if N.rounding_code(spec.rounding) == 5:
+            raise ValueError("QuantizePlan takes deterministic roundings; use quantize_into for 'sr'")
+        x = torch.empty(shape, dtype=dtype, device=device)
+        _require_cuda(x)
+        self.shape, self.dtype, self.spec = tuple(shape), dtype, spec
+        self.rows, self.K = x.reshape(-1, self.shape[-1]).shape
+        q, extras = quantize_into(x.zero_(), spec, want_values=want_values, want_codes=want_codes,
+                                  want_scale_codes=want_scale_codes, want_dequant=want_dequant)
+        self.qtensor, self.extras = q, extras
+        self.device = x.device
+        self._qs = _qspec(spec)
+        out = N.TcQuantOut()
+        out.values = 0 if q.values is None else q.values.data_ptr()
+        out.values_dtype = N.dtype_code(container_dtype(spec.format))
+        for name, t in (("scale", q.scale), ("zero_point", q.zero_point), ("global_scale", q.global_scale),
+                        ("codes", extras.codes), ("scale_codes", extras.scale_codes), ("dequant", extras.dequant)):
+            setattr(out, name, 0 if t is None else t.data_ptr())
+        self._out = out
+        lib = N.lib()
+        with torch.cuda.device(self.device):
+            ws_bytes = lib.tc_quantize_workspace(self.rows, self.K, self._qs)
+        self._ws = torch.empty(max(ws_bytes, 1), device=self.device, dtype=torch.uint8)
+        self._lib = lib
+
+    def run(self, x: torch.Tensor):
+        """Quantize ``x`` (the planned shape and dtype, contiguous, on the planned device) into the
+        plan's outputs on the current stream; returns ``(QTensor, QuantExtras)``."""
+        if tuple(x.shape) != self.shape or x.dtype != self.dtype or x.device != self.device or not x.is_contiguous():
+            raise ValueError("QuantizePlan.run needs a contiguous tensor of the planned shape, dtype and device")
+        N.check(self._lib.tc_quantize(x.data_ptr(), N.dtype_code(x.dtype), self.rows, self.K, self._qs, None, None,
+                                      None, self._out, self._ws.data_ptr(), self._ws.numel(),
+                                      N.stream_of(self.device)), "tc_quantize")
+        return self.qtensor, self.extras
+
+
 def quantize_triton(x: torch.Tensor, spec, *, amax: torch.Tensor | None = None, noise: torch.Tensor | None = None,
                     seed: int = 0, scale_noise: torch.Tensor | None = None):
     """Quantize onto ``spec`` (TriCast ``quantize_triton``): returns a QTensor whose values are in
