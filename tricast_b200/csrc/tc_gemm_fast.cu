@@ -14,6 +14,18 @@
 // enters through emax; it is the largest i + j such that some k has an A element of exponent
 // class >= i and a B element of class >= j, found with a few 16-bit mask ANDs per group.
 //
+// One pass, in fp64: each group's exact value is sx * 2**(es_a + es_b - srad - 2) with
+// sx = D * ms_a * ms_b (signed, |sx| < 2**20). Bound the labels from above per row and column of the
+// tile: L = es + (largest exponent class of that operand's group), emax'' = max(running exponent,
+// max_g L_a + max_g L_b) >= emax. If every group's value is a multiple of 2**(emax'' - F) (that is
+// min_g es_a + min_g es_b - srad - 2 >= emax'' - F) and the running value's bits survive the
+// alignment (emax'' - e_c <= F - 23), then no term is truncated under emax'' nor under emax, the
+// radix-F sum is the exact sum of the values, and with F <= 48 that sum (below 2**52 units) is exact
+// in an fp64 accumulator: the tile's result is the exact sum rounded toward zero to fp32 (the FDA
+// normalisation keeps min(F, 23) = 23 fraction bits and truncates subnormals), one conversion. A
+// thread whose tile fails the check redoes its outputs for that tile with the exact two-pass integer
+// labels and sums (mask records read from global memory), so the result is always the reference's.
+//
 // Operands are first encoded (encode_fp4_kernel) into 16-byte records per (K tile, group, row):
 // the sixteen int8 codes, the exponent-class masks, and the scale word. The GEMM kernel stages the
 // records of a 64-row x 64-column CTA tile through shared memory with 1-D TMA bulk copies
@@ -38,7 +50,8 @@ constexpr int kTileRows = 64;    // rows (A) / columns (B) per CTA
 constexpr int kStages = 4;
 constexpr int kNone = -(1 << 28);  // "no active term" exponent
 
-// Scale word: es (int16, biased by 0x8000 in bits 0..15), ms (bits 16..23), sign (bit 24).
+// Scale word: es (int16, biased by 0x8000 in bits 0..15), ms (bits 16..23), sign (bit 24), the
+// group's largest exponent class (bits 25..26) and "every code of the group is zero" (bit 27).
 __host__ __device__ __forceinline__ uint32_t pack_scale(int es, uint32_t ms, uint32_t neg) {
   return ((uint32_t)(es + 0x8000) & 0xFFFFu) | ((ms & 0xFFu) << 16) | ((neg & 1u) << 24);
 }
@@ -99,7 +112,8 @@ __global__ void __launch_bounds__(256) encode_fp4_kernel(EncodeArgs e) {
         float s = e.scale[r * e.nkd + k0 / e.kd];
         Term t = decode_term(s, e.sf);
         // Scale significands up to 4 bits (UE4M3, E4M3, E8M0) keep |D| * ms_a * ms_b < 2**20.
-        if (t.nan || t.inf || t.sig > 15 || t.exp < -30000 || t.exp > 30000) bad = true;
+        // |es| <= 400 keeps every fp64 power 2**(es_a + es_b - srad - 2) a normal number.
+        if (t.nan || t.inf || t.sig > 15 || t.exp < -400 || t.exp > 400) bad = true;
         zero = t.zero || (e.field0 && f2u(s) == 0x00400000u);
         es = t.exp;
         ms = (uint32_t)t.sig;
@@ -114,6 +128,10 @@ __global__ void __launch_bounds__(256) encode_fp4_kernel(EncodeArgs e) {
       } else {
         sword = pack_scale(es, ms, neg);
       }
+      const uint32_t gemax = c2 ? 2u : c1 ? 1u : 0u;
+      sword |= (gemax << 25) | ((c0 == 0 ? 1u : 0u) << 27);
+    } else {
+      sword |= 1u << 27;  // padding rows are all-zero groups
     }
     uint4 q4 = make_uint4(codes[0], codes[1], codes[2], codes[3]);
     uint4 m4;
@@ -135,6 +153,8 @@ struct GemmArgs {
   int64_t a_rows_pad, b_rows_pad;
   int64_t M, N, ntiles;
   int F, shift0;       // shift0 = F - 2 - srad (srad = radix of the combined scale)
+  int srad2;           // srad + 2: a group value is sx * 2**(es_a + es_b - srad2)
+  int pexp;            // 1023 - srad2: fp64 exponent field offset of those powers of two
   int rne;
   const float *alpha_a, *alpha_b, *bias;
   Fmt of;
@@ -147,12 +167,20 @@ struct GemmArgs {
 template <int NG>
 struct Stage {
   uint4 aq[NG][kTileRows];
-  uint4 am[NG][kTileRows];
   uint4 bq[NG][kTileRows];
-  uint4 bm[NG][kTileRows];
   uint32_t as[NG][kTileRows];
   uint32_t bs[NG][kTileRows];
 };
+
+constexpr int kBig = 1 << 28;
+
+// Upper bound of a group's exponent labels on one side: es + largest exponent class (kNone for an
+// all-zero group).
+__device__ __forceinline__ int side_label(uint32_t w) {
+  return (w >> 27) & 1u ? kNone : (int)(w & 0xFFFFu) - 0x8000 + (int)((w >> 25) & 3u);
+}
+// The group's scale exponent, kBig for an all-zero group (it constrains nothing).
+__device__ __forceinline__ int side_exp(uint32_t w) { return (w >> 27) & 1u ? kBig : (int)(w & 0xFFFFu) - 0x8000; }
 
 __device__ __forceinline__ int exp_class_max(const uint4 &a, const uint4 &b) {
   // a = {A0|A1<<16, A2|A1<<16, A2, A2}, b = {B1|B0<<16, B1|B2<<16, B0, B2|B1<<16}
@@ -206,7 +234,7 @@ __global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
   const int64_t m0 = (int64_t)blockIdx.y * kTileRows, n0 = (int64_t)blockIdx.x * kTileRows;
   constexpr uint32_t kRec = kTileRows * sizeof(uint4);
   constexpr uint32_t kSw = kTileRows * sizeof(uint32_t);
-  constexpr uint32_t kStageBytes = NG * (4 * kRec + 2 * kSw);
+  constexpr uint32_t kStageBytes = NG * (2 * kRec + 2 * kSw);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
@@ -221,10 +249,8 @@ __global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
       int64_t ga = (t * NG + gg) * g.a_rows_pad + m0;
       int64_t gb = (t * NG + gg) * g.b_rows_pad + n0;
       bulk_g2s(st.aq[gg], g.aq + ga, kRec, &full[s]);
-      bulk_g2s(st.am[gg], g.am + ga, kRec, &full[s]);
       bulk_g2s(st.as[gg], g.as + ga, kSw, &full[s]);
       bulk_g2s(st.bq[gg], g.bq + gb, kRec, &full[s]);
-      bulk_g2s(st.bm[gg], g.bm + gb, kRec, &full[s]);
       bulk_g2s(st.bs[gg], g.bs + gb, kSw, &full[s]);
     }
   };
@@ -248,76 +274,139 @@ __global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
       return;
     }
     const Stage<NG> &st = stages[s];
-    // Pass 1: exponent labels. emax starts at the running value's exponent (kNone if it is zero).
-    int emax[4][4];
+    // Per-row / per-column bounds over the tile's non-zero groups: max label, min scale exponent.
+    int max_la[4], min_ea[4], max_lb[4], min_eb[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int k = 0; k < 4; ++k) {
+      max_la[k] = max_lb[k] = kNone;
+      min_ea[k] = min_eb[k] = kBig;
+    }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) emax[i][j] = running_exp(c[i][j]);
-#pragma unroll 1
     for (int gg = 0; gg < NG; ++gg) {
-      uint4 bq[4], bm[4];
-      int eb[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        bq[j] = st.bq[gg][tx + 16 * j];
-        bm[j] = st.bm[gg][tx + 16 * j];
-        eb[j] = scale_exp(st.bs[gg][tx + 16 * j]);
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 aq = st.aq[gg][ty * 4 + i];
-        const uint4 am = st.am[gg][ty * 4 + i];
-        const int ea = scale_exp(st.as[gg][ty * 4 + i]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          int d = dot16(aq, bq[j]);
-          int label = exp_class_max(am, bm[j]) + ea + eb[j];
-          if (d != 0 && label > emax[i][j]) emax[i][j] = label;
-        }
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t wa = st.as[gg][ty * 4 + k], wb = st.bs[gg][tx + 16 * k];
+        max_la[k] = max(max_la[k], side_label(wa));
+        max_lb[k] = max(max_lb[k], side_label(wb));
+        min_ea[k] = min(min_ea[k], side_exp(wa));
+        min_eb[k] = min(min_eb[k], side_exp(wb));
       }
     }
-    // Pass 2: exact aligned sum at radix F (int64), starting from the running value's term.
-    int64_t total[4][4];
+    double tot[4][4];
+    bool safe = true;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) total[i][j] = running_term(c[i][j], g.F, emax[i][j]);
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
+        // Exponent of the running value: none for zero (and for Inf / NaN, which stay as they are);
+        // a subnormal running value takes the exact path.
+        const int ec = (cb == 0 || cb >= kInf) ? kNone : cb < 0x00800000u ? kBig : (int)(cb >> 23) - 127;
+        const int em = max(ec, max_la[i] + max_lb[j]);
+        safe &= min_ea[i] + min_eb[j] - g.srad2 >= em - g.F;
+        safe &= ec == kNone || em - ec <= g.F - 23;
+        tot[i][j] = (double)c[i][j];
+      }
 #pragma unroll 1
     for (int gg = 0; gg < NG; ++gg) {
       uint4 bq[4];
-      uint32_t sb[4];
+      int mb[4];
+      uint32_t pb[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         bq[j] = st.bq[gg][tx + 16 * j];
-        sb[j] = st.bs[gg][tx + 16 * j];
+        const uint32_t w = st.bs[gg][tx + 16 * j];
+        const int ms = (int)((w >> 16) & 0xFFu);
+        mb[j] = (w >> 24) & 1u ? -ms : ms;
+        pb[j] = (uint32_t)scale_exp(w) << 20;
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint4 aq = st.aq[gg][ty * 4 + i];
-        const uint32_t sa = st.as[gg][ty * 4 + i];
+        const uint32_t w = st.as[gg][ty * 4 + i];
+        const int ms = (int)((w >> 16) & 0xFFu);
+        const int ma = (w >> 24) & 1u ? -ms : ms;
+        const uint32_t pa = ((uint32_t)(scale_exp(w) + g.pexp) << 20);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          int d = dot16(aq, bq[j]);
-          uint32_t x = (uint32_t)(d < 0 ? -d : d) * (((sa >> 16) & 0xFFu) * ((sb[j] >> 16) & 0xFFu));
-          int sh = g.shift0 + scale_exp(sa) + scale_exp(sb[j]) - emax[i][j];
-          // x < 2**20 and sh <= shift0 <= 40: (x << 40) >> (40 - sh) is the exact truncation.
-          int r = max(40 - sh, 0);  // sh > 40 only for d == 0 (x == 0)
-          uint64_t v = r >= 64 ? 0ull : (((uint64_t)x << 40) >> r);
-          bool neg = (d < 0) != (((sa ^ sb[j]) >> 24) & 1u);
-          total[i][j] += neg ? -(int64_t)v : (int64_t)v;
+          const int d = dot16(aq, bq[j]);
+          // 2**52 + sx + 2**20 as an fp64 bit pattern, minus 2**52 + 2**20: sx exactly.
+          const uint32_t u = (uint32_t)(d * (ma * mb[j]) + (1 << 20));
+          const double sx = __dadd_rn(__hiloint2double(0x43300000, (int)u), -(0x1p52 + 0x1p20));
+          tot[i][j] = __fma_rn(sx, __hiloint2double((int)(pa + pb[j]), 0), tot[i][j]);
         }
       }
     }
+    if (!safe) {
+      // Exact two-pass labels and sums for this thread's outputs (mask records from global memory).
+      int emax[4][4];
+      int64_t total[4][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
-        if (cb >= kInf) continue;                 // Inf/NaN running value is sticky
-        if (emax[i][j] == kNone) continue;        // every term zero: keep c
-        c[i][j] = fixed_to_fp32(total[i][j], emax[i][j], g.F, g.rne, true);
+        for (int j = 0; j < 4; ++j) emax[i][j] = running_exp(c[i][j]);
+#pragma unroll 1
+      for (int gg = 0; gg < NG; ++gg) {
+        const int64_t grow = (t * NG + gg);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 aq = st.aq[gg][ty * 4 + i];
+          const uint4 am = g.am[grow * g.a_rows_pad + m0 + ty * 4 + i];
+          const int ea = scale_exp(st.as[gg][ty * 4 + i]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 bm = g.bm[grow * g.b_rows_pad + n0 + tx + 16 * j];
+            const int d = dot16(aq, st.bq[gg][tx + 16 * j]);
+            const int label = exp_class_max(am, bm) + ea + scale_exp(st.bs[gg][tx + 16 * j]);
+            if (d != 0 && label > emax[i][j]) emax[i][j] = label;
+          }
+        }
       }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) total[i][j] = running_term(c[i][j], g.F, emax[i][j]);
+#pragma unroll 1
+      for (int gg = 0; gg < NG; ++gg) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 aq = st.aq[gg][ty * 4 + i];
+          const uint32_t sa = st.as[gg][ty * 4 + i];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t sbj = st.bs[gg][tx + 16 * j];
+            const int d = dot16(aq, st.bq[gg][tx + 16 * j]);
+            const uint32_t x = (uint32_t)(d < 0 ? -d : d) * (((sa >> 16) & 0xFFu) * ((sbj >> 16) & 0xFFu));
+            const int sh = g.shift0 + scale_exp(sa) + scale_exp(sbj) - emax[i][j];
+            // x < 2**20 and sh <= shift0 <= 40: (x << 40) >> (40 - sh) is the exact truncation.
+            const int r = max(40 - sh, 0);  // sh > 40 only for d == 0 (x == 0)
+            const uint64_t v = r >= 64 ? 0ull : (((uint64_t)x << 40) >> r);
+            const bool neg = (d < 0) != (((sa ^ sbj) >> 24) & 1u);
+            total[i][j] += neg ? -(int64_t)v : (int64_t)v;
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
+          if (cb >= kInf || emax[i][j] == kNone) continue;  // sticky Inf/NaN; every term zero keeps c
+          c[i][j] = fixed_to_fp32(total[i][j], emax[i][j], g.F, g.rne, true);
+        }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
+          if (cb >= kInf) continue;  // sticky Inf/NaN
+          const double v = tot[i][j];
+          float r = (g.rne && fabs(v) >= 0x1p-126) ? __double2float_rn(v) : __double2float_rz(v);
+          if (fabs(v) >= 0x1p128) r = v > 0 ? INFINITY : -INFINITY;
+          c[i][j] = r;
+        }
+    }
     __syncthreads();  // everyone is done with stage s
     if (threadIdx.x == 0 && t + kStages < g.ntiles) issue(t + kStages, s);
   }
@@ -363,6 +452,7 @@ static Fp4Plan plan_fp4(const GemmDesc &g) {
   int srad = (g.a.skind == SK_K ? g.a.srad : 0) + (g.b.skind == SK_K ? g.b.srad : 0);
   int shift0 = g.F - 2 - srad;
   if (shift0 > 40 || shift0 < -20) return p;
+  if (g.F < 23 || g.F > 48) return p;  // the fp64 single pass needs 23 <= F (normalisation) and F <= 48
   p.ng = g.KT / fp4::kGS;
   if (p.ng != 1 && p.ng != 2 && p.ng != 4 && p.ng != 8) return p;
   p.ntiles = (g.K + g.KT - 1) / g.KT;
@@ -462,6 +552,8 @@ int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
   a.F = g.F;
   int srad = (g.a.skind == SK_K ? g.a.srad : 0) + (g.b.skind == SK_K ? g.b.srad : 0);
   a.shift0 = g.F - 2 - srad;
+  a.srad2 = srad + 2;
+  a.pexp = 1023 - (srad + 2);
   a.rne = g.rne;
   a.alpha_a = g.a.alpha;
   a.alpha_b = g.b.alpha;
