@@ -155,6 +155,63 @@ def test_fp4_fast_path_falls_back_on_specials():
     assert bits_equal(got, _oracle_gemm(a, b, spec))
 
 
+E2M1_GRID = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], np.float32)
+
+
+def _fp4_operand(values: np.ndarray, scales: np.ndarray, scale_fmt: str, kd: int) -> Operand:
+    from tricast_b200.formats import get_format
+
+    return Operand(torch.from_numpy(values).cuda(), get_format("fp4_e2m1"), torch.from_numpy(scales).cuda(),
+                   get_format(scale_fmt), "k", kd)
+
+
+@pytest.mark.parametrize("case", ["wide_tile_scales", "cancel_then_large", "tiny_running_nvfp4", "zero_rows"])
+def test_fp4_single_pass_and_exact_fallback(case):
+    """The fp64 single pass of the GDFS FP4 kernel and its exact two-pass fallback: K-tiles whose group
+    scales span more than the radix allows, running values that cancel to (almost) nothing before far
+    larger terms arrive (the reference truncates the running value then), and all-zero rows."""
+    rng = np.random.default_rng(len(case) * 7919)
+    M, N, K = 48, 40, 512
+    kd, sfmt = (16, "ue4m3") if case == "tiny_running_nvfp4" else (32, "e8m0")
+    va = E2M1_GRID[rng.integers(0, 8, (M, K))] * rng.choice([-1.0, 1.0], (M, K)).astype(np.float32)
+    vb = E2M1_GRID[rng.integers(0, 8, (N, K))] * rng.choice([-1.0, 1.0], (N, K)).astype(np.float32)
+    ga, gb = K // kd, K // kd
+    if sfmt == "e8m0":
+        ea = rng.integers(-4, 5, (M, ga))
+        eb = rng.integers(-4, 5, (N, gb))
+    else:
+        ea = rng.integers(-6, 7, (M, ga))
+        eb = rng.integers(-6, 7, (N, gb))
+    if case == "wide_tile_scales":
+        ea[::3] += rng.integers(-50, 51, ea[::3].shape)   # > 40 binades inside a 64-wide tile
+    if case in ("cancel_then_large", "tiny_running_nvfp4"):
+        # Tile 1 repeats tile 0 with the sign flipped on half the rows (B repeats too): the running
+        # value returns to (almost) zero; a few elements of tile 1 differ by one grid step so that
+        # some outputs keep a tiny remainder; later tiles carry far larger scales.
+        vb[:, 64:128] = vb[:, 0:64]
+        eb[:, 64 // kd:128 // kd] = eb[:, 0:64 // kd]
+        va[::2, 64:128] = -va[::2, 0:64]
+        ea[::2, 64 // kd:128 // kd] = ea[::2, 0:64 // kd]
+        va[::4, 64 + 5] = np.where(va[::4, 64 + 5] == 0, 0.5, va[::4, 64 + 5])
+        big = 20 if sfmt == "e8m0" else 6
+        ea[:, 128 // kd:] += big
+    if case == "zero_rows":
+        va[5] = 0.0
+        vb[7, :256] = 0.0
+    if sfmt == "e8m0":
+        sa = np.exp2(np.clip(ea, -127, 127)).astype(np.float32)
+        sb = np.exp2(np.clip(eb, -127, 127)).astype(np.float32)
+    else:  # UE4M3 grid: m/8 * 2**e with m in 8..15, e in [-6, 7] (max_normal 448)
+        sa = ((8 + rng.integers(0, 8, ea.shape)) / 8.0 * np.exp2(np.clip(ea, -6, 7))).astype(np.float32)
+        sb = ((8 + rng.integers(0, 8, eb.shape)) / 8.0 * np.exp2(np.clip(eb, -6, 7))).astype(np.float32)
+    a, b = _fp4_operand(va, sa, sfmt, kd), _fp4_operand(vb, sb, sfmt, kd)
+    for spec in (PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32"),
+                 PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32", norm_rounding="rne")):
+        got = gemm_triton(a, b, spec).cpu().numpy()
+        want = _oracle_gemm(a, b, spec)
+        assert bits_equal(got, want), f"{case} {spec.norm_rounding}: {first_mismatch(got, want)}"
+
+
 @pytest.mark.parametrize("shape", [(37, 70, 200), (1, 1, 5), (130, 65, 1040), (64, 64, 8192)])
 @pytest.mark.parametrize("preset,scheme", [
     ("nvidia_hopper_fp8", "fp8_tensor"), ("nvidia_ada_fp8", "fp8_tensor"), ("nvidia_hopper_fp8", "mxfp8_e4m3"),

@@ -14,17 +14,20 @@
 // enters through emax; it is the largest i + j such that some k has an A element of exponent
 // class >= i and a B element of class >= j, found with a few 16-bit mask ANDs per group.
 //
-// One pass, in fp64: each group's exact value is sx * 2**(es_a + es_b - srad - 2) with
-// sx = D * ms_a * ms_b (signed, |sx| < 2**20). Bound the labels from above per row and column of the
-// tile: L = es + (largest exponent class of that operand's group), emax'' = max(running exponent,
-// max_g L_a + max_g L_b) >= emax. If every group's value is a multiple of 2**(emax'' - F) (that is
-// min_g es_a + min_g es_b - srad - 2 >= emax'' - F) and the running value's bits survive the
-// alignment (emax'' - e_c <= F - 23), then no term is truncated under emax'' nor under emax, the
-// radix-F sum is the exact sum of the values, and with F <= 48 that sum (below 2**52 units) is exact
-// in an fp64 accumulator: the tile's result is the exact sum rounded toward zero to fp32 (the FDA
-// normalisation keeps min(F, 23) = 23 fraction bits and truncates subnormals), one conversion. A
-// thread whose tile fails the check redoes its outputs for that tile with the exact two-pass integer
-// labels and sums (mask records read from global memory), so the result is always the reference's.
+// One pass. Bound the labels from above per row and column of the tile: L = es + (largest exponent
+// class of that operand's group), emax'' = max(running exponent, max_g L_a + max_g L_b) >= emax. If
+// every group's value sx * 2**(es_a + es_b - srad - 2) (sx = D * ms_a * ms_b, |sx| < 2**20) is a
+// multiple of 2**(emax'' - F) (min_g es_a + min_g es_b - srad - 2 >= emax'' - F) and the running
+// value's bits survive the alignment (emax'' - e_c <= F - 23), then no term is truncated under
+// emax'' nor under emax, and the radix-F sum is the exact sum of the values. That sum is formed in
+// integers: relative to the row's and column's smallest scale exponents each group contributes
+// D * (ms_a << (es_a - min es_a)) * (ms_b << (es_b - min es_b)), two multiply-adds into an int64
+// (the exponent spread is checked to keep it below 2**45); once per tile the int64 becomes an fp64
+// (exact), is scaled by 2**(min es_a + min es_b - srad - 2) and added to the running value (exact for
+// F <= 48), and the result rounded toward zero to fp32 is the FDA normalisation (min(F, 23) = 23
+// fraction bits, subnormals truncated). A thread whose tile fails a check redoes its outputs for that
+// tile with the exact two-pass integer labels and sums (mask records read from global memory), so the
+// result is always the reference's.
 //
 // Operands are first encoded (encode_fp4_kernel) into 16-byte records per (K tile, group, row):
 // the sixteen int8 codes, the exponent-class masks, and the scale word. The GEMM kernel stages the
@@ -35,6 +38,7 @@
 // Any operand value or scale the fast path cannot take (NaN/Inf, off-grid values, wide scale
 // significands) raises a device flag during encoding; the fast kernel then writes nothing and the
 // exact generic kernel, launched behind it on the same stream, computes the product instead.
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -49,6 +53,7 @@ constexpr int kGS = 16;          // GDFS group size of the fast path
 constexpr int kTileRows = 64;    // rows (A) / columns (B) per CTA
 constexpr int kStages = 4;
 constexpr int kNone = -(1 << 28);  // "no active term" exponent
+constexpr int kBig = 1 << 28;
 
 // Scale word: es (int16, biased by 0x8000 in bits 0..15), ms (bits 16..23), sign (bit 24), the
 // group's largest exponent class (bits 25..26) and "every code of the group is zero" (bit 27).
@@ -147,9 +152,47 @@ __global__ void __launch_bounds__(256) encode_fp4_kernel(EncodeArgs e) {
   if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicExch(e.flag, 1);
 }
 
+// Per (K tile, row): the multipliers D is scaled by and the tile's bounds. For the tile's non-zero
+// groups let minE = min es and L = max(es + largest exponent class); a group's multiplier is
+// +-(ms << (es - minE)) (0 for an all-zero group). tw = {minE, L}: {kBig, kNone} when every group is
+// zero, L = kBig when the exponent spread exceeds 11 (the multiplier bound), which forces the exact
+// path for every output that uses the row.
+__global__ void __launch_bounds__(256) tile_words_kernel(const uint32_t *__restrict__ sw, int64_t rows_pad,
+                                                         int64_t ntiles, int ng, int32_t *__restrict__ mult,
+                                                         int2 *__restrict__ tw) {
+  const int64_t total = ntiles * rows_pad;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = idx / rows_pad, r = idx % rows_pad;
+    int min_e = kBig, max_e = kNone, max_l = kNone;
+    for (int gg = 0; gg < ng; ++gg) {
+      const uint32_t w = sw[(t * ng + gg) * rows_pad + r];
+      if ((w >> 27) & 1u) continue;
+      const int es = (int)(w & 0xFFFFu) - 0x8000;
+      min_e = min(min_e, es);
+      max_e = max(max_e, es);
+      max_l = max(max_l, es + (int)((w >> 25) & 3u));
+    }
+    const bool wide = min_e != kBig && max_e - min_e > 11;
+    for (int gg = 0; gg < ng; ++gg) {
+      const int64_t gi = (t * ng + gg) * rows_pad + r;
+      const uint32_t w = sw[gi];
+      int m = 0;
+      if (!((w >> 27) & 1u) && !wide) {
+        m = (int)((w >> 16) & 0xFFu) << ((int)(w & 0xFFFFu) - 0x8000 - min_e);
+        if ((w >> 24) & 1u) m = -m;
+      }
+      mult[gi] = m;
+    }
+    tw[idx] = make_int2(min_e, wide ? kBig : max_l);
+  }
+}
+
 struct GemmArgs {
   const uint4 *aq, *am, *bq, *bm;
-  const uint32_t *as, *bs;
+  const uint32_t *as, *bs;        // scale words (exact path)
+  const int32_t *amul, *bmul;     // multipliers [ntiles * ng][rows_pad]
+  const int2 *atw, *btw;          // tile words [ntiles][rows_pad]
   int64_t a_rows_pad, b_rows_pad;
   int64_t M, N, ntiles;
   int F, shift0;       // shift0 = F - 2 - srad (srad = radix of the combined scale)
@@ -168,19 +211,12 @@ template <int NG>
 struct Stage {
   uint4 aq[NG][kTileRows];
   uint4 bq[NG][kTileRows];
-  uint32_t as[NG][kTileRows];
-  uint32_t bs[NG][kTileRows];
+  int32_t amul[NG][kTileRows];
+  int32_t bmul[NG][kTileRows];
+  int2 atw[kTileRows];
+  int2 btw[kTileRows];
 };
 
-constexpr int kBig = 1 << 28;
-
-// Upper bound of a group's exponent labels on one side: es + largest exponent class (kNone for an
-// all-zero group).
-__device__ __forceinline__ int side_label(uint32_t w) {
-  return (w >> 27) & 1u ? kNone : (int)(w & 0xFFFFu) - 0x8000 + (int)((w >> 25) & 3u);
-}
-// The group's scale exponent, kBig for an all-zero group (it constrains nothing).
-__device__ __forceinline__ int side_exp(uint32_t w) { return (w >> 27) & 1u ? kBig : (int)(w & 0xFFFFu) - 0x8000; }
 
 __device__ __forceinline__ int exp_class_max(const uint4 &a, const uint4 &b) {
   // a = {A0|A1<<16, A2|A1<<16, A2, A2}, b = {B1|B0<<16, B1|B2<<16, B0, B2|B1<<16}
@@ -234,7 +270,8 @@ __global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
   const int64_t m0 = (int64_t)blockIdx.y * kTileRows, n0 = (int64_t)blockIdx.x * kTileRows;
   constexpr uint32_t kRec = kTileRows * sizeof(uint4);
   constexpr uint32_t kSw = kTileRows * sizeof(uint32_t);
-  constexpr uint32_t kStageBytes = NG * (2 * kRec + 2 * kSw);
+  constexpr uint32_t kTw = kTileRows * sizeof(int2);
+  constexpr uint32_t kStageBytes = NG * (2 * kRec + 2 * kSw) + 2 * kTw;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
@@ -249,10 +286,12 @@ __global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
       int64_t ga = (t * NG + gg) * g.a_rows_pad + m0;
       int64_t gb = (t * NG + gg) * g.b_rows_pad + n0;
       bulk_g2s(st.aq[gg], g.aq + ga, kRec, &full[s]);
-      bulk_g2s(st.as[gg], g.as + ga, kSw, &full[s]);
+      bulk_g2s(st.amul[gg], g.amul + ga, kSw, &full[s]);
       bulk_g2s(st.bq[gg], g.bq + gb, kRec, &full[s]);
-      bulk_g2s(st.bs[gg], g.bs + gb, kSw, &full[s]);
+      bulk_g2s(st.bmul[gg], g.bmul + gb, kSw, &full[s]);
     }
+    bulk_g2s(st.atw, g.atw + t * g.a_rows_pad + m0, kTw, &full[s]);
+    bulk_g2s(st.btw, g.btw + t * g.b_rows_pad + n0, kTw, &full[s]);
   };
   if (threadIdx.x == 0)
     for (int s = 0; s < kStages && s < g.ntiles; ++s) issue(s, s);
@@ -274,67 +313,54 @@ __global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
       return;
     }
     const Stage<NG> &st = stages[s];
-    // Per-row / per-column bounds over the tile's non-zero groups: max label, min scale exponent.
-    int max_la[4], min_ea[4], max_lb[4], min_eb[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      max_la[k] = max_lb[k] = kNone;
-      min_ea[k] = min_eb[k] = kBig;
-    }
-#pragma unroll
-    for (int gg = 0; gg < NG; ++gg) {
+    // Bounds from the tile words: rows i (A) and columns j (B) of this thread.
+    int min_ea[4], max_la[4], min_eb[4], max_lb[4];
+    int sep = kBig;  // min_i (min es_a - L_a) + min_j (min es_b - L_b), separable part of the check
+    {
+      int da = kBig, db = kBig;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const uint32_t wa = st.as[gg][ty * 4 + k], wb = st.bs[gg][tx + 16 * k];
-        max_la[k] = max(max_la[k], side_label(wa));
-        max_lb[k] = max(max_lb[k], side_label(wb));
-        min_ea[k] = min(min_ea[k], side_exp(wa));
-        min_eb[k] = min(min_eb[k], side_exp(wb));
+        const int2 wa = st.atw[ty * 4 + k], wb = st.btw[tx + 16 * k];
+        min_ea[k] = wa.x; max_la[k] = wa.y;
+        min_eb[k] = wb.x; max_lb[k] = wb.y;
+        da = min(da, wa.x - wa.y);
+        db = min(db, wb.x - wb.y);
       }
+      sep = da + db;
     }
-    double tot[4][4];
-    bool safe = true;
+    // No term truncated under emax'' = max(e_c, L_a + L_b): every group's value is a multiple of
+    // 2**(emax'' - F) and the running value keeps its bits, i.e. (with e_c the running exponent)
+    //   min es_a + min es_b - srad - 2 >= L_a + L_b - F      (separable: sep >= srad + 2 - F)
+    //   L_a + L_b - (F - 23) <= e_c <= min es_a + min es_b + F - srad - 2   (running value non-zero)
+    bool safe = sep >= g.srad2 - g.F;
+    int64_t acc[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
-        // Exponent of the running value: none for zero (and for Inf / NaN, which stay as they are);
-        // a subnormal running value takes the exact path.
-        const int ec = (cb == 0 || cb >= kInf) ? kNone : cb < 0x00800000u ? kBig : (int)(cb >> 23) - 127;
-        const int em = max(ec, max_la[i] + max_lb[j]);
-        safe &= min_ea[i] + min_eb[j] - g.srad2 >= em - g.F;
-        safe &= ec == kNone || em - ec <= g.F - 23;
-        tot[i][j] = (double)c[i][j];
+        if (cb != 0 && cb < kInf) {
+          // A subnormal running value takes the exact path.
+          const int ec = cb < 0x00800000u ? kNone : (int)(cb >> 23) - 127;
+          safe &= ec >= max_la[i] + max_lb[j] - (g.F - 23) && ec <= min_ea[i] + min_eb[j] + g.F - g.srad2;
+        }
+        acc[i][j] = 0;
       }
 #pragma unroll 1
     for (int gg = 0; gg < NG; ++gg) {
       uint4 bq[4];
       int mb[4];
-      uint32_t pb[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         bq[j] = st.bq[gg][tx + 16 * j];
-        const uint32_t w = st.bs[gg][tx + 16 * j];
-        const int ms = (int)((w >> 16) & 0xFFu);
-        mb[j] = (w >> 24) & 1u ? -ms : ms;
-        pb[j] = (uint32_t)scale_exp(w) << 20;
+        mb[j] = st.bmul[gg][tx + 16 * j];
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint4 aq = st.aq[gg][ty * 4 + i];
-        const uint32_t w = st.as[gg][ty * 4 + i];
-        const int ms = (int)((w >> 16) & 0xFFu);
-        const int ma = (w >> 24) & 1u ? -ms : ms;
-        const uint32_t pa = ((uint32_t)(scale_exp(w) + g.pexp) << 20);
+        const int ma = st.amul[gg][ty * 4 + i];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int d = dot16(aq, bq[j]);
-          // 2**52 + sx + 2**20 as an fp64 bit pattern, minus 2**52 + 2**20: sx exactly.
-          const uint32_t u = (uint32_t)(d * (ma * mb[j]) + (1 << 20));
-          const double sx = __dadd_rn(__hiloint2double(0x43300000, (int)u), -(0x1p52 + 0x1p20));
-          tot[i][j] = __fma_rn(sx, __hiloint2double((int)(pa + pb[j]), 0), tot[i][j]);
-        }
+        for (int j = 0; j < 4; ++j) acc[i][j] += (int64_t)dot16(aq, bq[j]) * (int64_t)(ma * mb[j]);
       }
     }
     if (!safe) {
@@ -352,12 +378,12 @@ __global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
         for (int i = 0; i < 4; ++i) {
           const uint4 aq = st.aq[gg][ty * 4 + i];
           const uint4 am = g.am[grow * g.a_rows_pad + m0 + ty * 4 + i];
-          const int ea = scale_exp(st.as[gg][ty * 4 + i]);
+          const int ea = scale_exp(g.as[grow * g.a_rows_pad + m0 + ty * 4 + i]);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint4 bm = g.bm[grow * g.b_rows_pad + n0 + tx + 16 * j];
             const int d = dot16(aq, st.bq[gg][tx + 16 * j]);
-            const int label = exp_class_max(am, bm) + ea + scale_exp(st.bs[gg][tx + 16 * j]);
+            const int label = exp_class_max(am, bm) + ea + scale_exp(g.bs[grow * g.b_rows_pad + n0 + tx + 16 * j]);
             if (d != 0 && label > emax[i][j]) emax[i][j] = label;
           }
         }
@@ -368,13 +394,14 @@ __global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
         for (int j = 0; j < 4; ++j) total[i][j] = running_term(c[i][j], g.F, emax[i][j]);
 #pragma unroll 1
       for (int gg = 0; gg < NG; ++gg) {
+        const int64_t grow = (t * NG + gg);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const uint4 aq = st.aq[gg][ty * 4 + i];
-          const uint32_t sa = st.as[gg][ty * 4 + i];
+          const uint32_t sa = g.as[grow * g.a_rows_pad + m0 + ty * 4 + i];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint32_t sbj = st.bs[gg][tx + 16 * j];
+            const uint32_t sbj = g.bs[grow * g.b_rows_pad + n0 + tx + 16 * j];
             const int d = dot16(aq, st.bq[gg][tx + 16 * j]);
             const uint32_t x = (uint32_t)(d < 0 ? -d : d) * (((sa >> 16) & 0xFFu) * ((sbj >> 16) & 0xFFu));
             const int sh = g.shift0 + scale_exp(sa) + scale_exp(sbj) - emax[i][j];
@@ -401,7 +428,10 @@ __global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
         for (int j = 0; j < 4; ++j) {
           const uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
           if (cb >= kInf) continue;  // sticky Inf/NaN
-          const double v = tot[i][j];
+          // c + acc * 2**(min es_a + min es_b - srad - 2), exact in fp64.
+          const int e2 = min_ea[i] + min_eb[j] - g.srad2;
+          const double p2 = __hiloint2double(min_ea[i] < kBig && min_eb[j] < kBig ? (e2 + 1023) << 20 : 0, 0);
+          const double v = __fma_rn((double)acc[i][j], p2, (double)c[i][j]);
           float r = (g.rne && fabs(v) >= 0x1p-126) ? __double2float_rn(v) : __double2float_rz(v);
           if (fabs(v) >= 0x1p128) r = v > 0 ? INFINITY : -INFINITY;
           c[i][j] = r;
@@ -436,7 +466,8 @@ struct Fp4Plan {
   bool ok;
   int ng;
   int64_t ntiles, a_pad, b_pad;
-  size_t off[6], bytes[6], flag_off, total;
+  // per side (A then B): codes, masks, scale words, multipliers, tile words
+  size_t off[10], bytes[10], flag_off, total;
 };
 
 static bool is_e2m1(const Fmt &f) { return f.kind == 0 && f.mbits == 1 && f.emin == 0 && f.emax == 2 && f.is_signed; }
@@ -459,9 +490,10 @@ static Fp4Plan plan_fp4(const GemmDesc &g) {
   p.a_pad = (g.M + fp4::kTileRows - 1) / fp4::kTileRows * fp4::kTileRows;
   p.b_pad = (g.N + fp4::kTileRows - 1) / fp4::kTileRows * fp4::kTileRows;
   int64_t ga = p.ntiles * p.ng * p.a_pad, gb = p.ntiles * p.ng * p.b_pad;
-  size_t sizes[6] = {(size_t)ga * 16, (size_t)ga * 16, (size_t)ga * 4, (size_t)gb * 16, (size_t)gb * 16, (size_t)gb * 4};
+  size_t sizes[10] = {(size_t)ga * 16, (size_t)ga * 16, (size_t)ga * 4, (size_t)ga * 4, (size_t)(p.ntiles * p.a_pad) * 8,
+                      (size_t)gb * 16, (size_t)gb * 16, (size_t)gb * 4, (size_t)gb * 4, (size_t)(p.ntiles * p.b_pad) * 8};
   size_t off = 0;
-  for (int i = 0; i < 6; ++i) {
+  for (int i = 0; i < 10; ++i) {
     p.off[i] = off;
     p.bytes[i] = sizes[i];
     off += (sizes[i] + 255) & ~(size_t)255;
@@ -526,9 +558,9 @@ int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
     e.kd = o.kd;
     e.sf = o.sf;
     e.field0 = o.field0;
-    e.q = reinterpret_cast<uint4 *>(ws + p.off[side * 3 + 0]);
-    e.m = reinterpret_cast<uint4 *>(ws + p.off[side * 3 + 1]);
-    e.s = reinterpret_cast<uint32_t *>(ws + p.off[side * 3 + 2]);
+    e.q = reinterpret_cast<uint4 *>(ws + p.off[side * 5 + 0]);
+    e.m = reinterpret_cast<uint4 *>(ws + p.off[side * 5 + 1]);
+    e.s = reinterpret_cast<uint32_t *>(ws + p.off[side * 5 + 2]);
     e.flag = flag;
     e.side = side;
     int64_t work = p.ntiles * p.ng * e.rows_pad;
@@ -536,14 +568,24 @@ int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
     if (blocks > 148 * 16) blocks = 148 * 16;
     fp4::encode_fp4_kernel<<<(unsigned)blocks, 256, 0, s>>>(e);
     count_launch();
+    const int64_t twork = p.ntiles * e.rows_pad;
+    const int64_t tblocks = std::min<int64_t>((twork + 255) / 256, 148 * 16);
+    fp4::tile_words_kernel<<<(unsigned)tblocks, 256, 0, s>>>(e.s, e.rows_pad, p.ntiles, p.ng,
+                                                             reinterpret_cast<int32_t *>(ws + p.off[side * 5 + 3]),
+                                                             reinterpret_cast<int2 *>(ws + p.off[side * 5 + 4]));
+    count_launch();
   }
   fp4::GemmArgs a;
   a.aq = reinterpret_cast<const uint4 *>(ws + p.off[0]);
   a.am = reinterpret_cast<const uint4 *>(ws + p.off[1]);
   a.as = reinterpret_cast<const uint32_t *>(ws + p.off[2]);
-  a.bq = reinterpret_cast<const uint4 *>(ws + p.off[3]);
-  a.bm = reinterpret_cast<const uint4 *>(ws + p.off[4]);
-  a.bs = reinterpret_cast<const uint32_t *>(ws + p.off[5]);
+  a.amul = reinterpret_cast<const int32_t *>(ws + p.off[3]);
+  a.atw = reinterpret_cast<const int2 *>(ws + p.off[4]);
+  a.bq = reinterpret_cast<const uint4 *>(ws + p.off[5]);
+  a.bm = reinterpret_cast<const uint4 *>(ws + p.off[6]);
+  a.bs = reinterpret_cast<const uint32_t *>(ws + p.off[7]);
+  a.bmul = reinterpret_cast<const int32_t *>(ws + p.off[8]);
+  a.btw = reinterpret_cast<const int2 *>(ws + p.off[9]);
   a.a_rows_pad = p.a_pad;
   a.b_rows_pad = p.b_pad;
   a.M = g.M;
