@@ -260,12 +260,13 @@ __device__ __forceinline__ int64_t running_term(float c, int F, int emax) {
 }
 
 // 256 threads as 16 x 16; thread (ty, tx) owns rows ty*4 + i and columns tx + 16*j of the tile.
-template <int NG>
-__global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
+template <int NG, bool RNE>
+__global__ void __launch_bounds__(256, 2) gdfs_fp4_kernel(GemmArgs g) {
   if (*g.flag) return;  // the generic kernel takes over
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Stage<NG> *stages = reinterpret_cast<Stage<NG> *>(smem_raw);
-  __shared__ __align__(8) uint64_t full[kStages];
+  __shared__ __align__(8) uint64_t full[kStages];   // stage landed (bulk copies complete)
+  __shared__ __align__(8) uint64_t empty[kStages];  // every warp is done with the stage
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int64_t m0 = (int64_t)blockIdx.y * kTileRows, n0 = (int64_t)blockIdx.x * kTileRows;
   constexpr uint32_t kRec = kTileRows * sizeof(uint4);
@@ -274,12 +275,17 @@ __global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
   constexpr uint32_t kStageBytes = NG * (2 * kRec + 2 * kSw) + 2 * kTw;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);
+    }
     fence_barrier_init();
   }
   __syncthreads();
 
+  int64_t issued = 0;  // tiles handed to the copy engine (thread 0's count)
   auto issue = [&](int64_t t, int s) {
+    issued = t + 1;
     Stage<NG> &st = stages[s];
     mbar_expect_tx(&full[s], kStageBytes);
     for (int gg = 0; gg < NG; ++gg) {
@@ -302,15 +308,18 @@ __global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) c[i][j] = 0.0f;
 
-  bool timed_out = false;
-  for (int64_t t = 0; t < g.ntiles; ++t) {
+  // Warps run independently through the ring: a warp releases a stage on empty[s]; thread 0 refills
+  // the stage of tile t - 1 once all eight warps have released it. Every wait is bounded; a warp
+  // whose wait runs out sets the status word (the exact kernel behind this one then recomputes the
+  // product) and leaves the loop.
+  bool producer_ok = true;
+  int64_t t = 0;
+  for (; t < g.ntiles; ++t) {
     const int s = (int)(t % kStages);
-    if (!mbar_wait(&full[s], (uint32_t)((t / kStages) & 1))) {
-      timed_out = true;
-    }
-    if (__syncthreads_or(timed_out)) {
-      if (threadIdx.x == 0) atomicExch(g.status, 1);
-      return;
+    const bool landed = mbar_wait(&full[s], (uint32_t)((t / kStages) & 1));
+    if (__any_sync(0xFFFFFFFFu, !landed)) {
+      if ((threadIdx.x & 31) == 0) atomicExch(g.status, 1);
+      break;
     }
     const Stage<NG> &st = stages[s];
     // Bounds from the tile words: rows i (A) and columns j (B) of this thread.
@@ -338,12 +347,13 @@ __global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
+        // In biased form: lo <= biased exponent of c <= hi, or c is zero / Inf / NaN. A subnormal
+        // running value (biased exponent 0 < lo) takes the exact path.
         const uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
-        if (cb != 0 && cb < kInf) {
-          // A subnormal running value takes the exact path.
-          const int ec = cb < 0x00800000u ? kNone : (int)(cb >> 23) - 127;
-          safe &= ec >= max_la[i] + max_lb[j] - (g.F - 23) && ec <= min_ea[i] + min_eb[j] + g.F - g.srad2;
-        }
+        const int be = (int)(cb >> 23);
+        const int lo = max(max_la[i] + max_lb[j] - (g.F - 23) + 127, 1);
+        const int hi = min_ea[i] + min_eb[j] + g.F - g.srad2 + 127;
+        safe &= (cb == 0) | (cb >= kInf) | ((be >= lo) & (be <= hi));
         acc[i][j] = 0;
       }
 #pragma unroll 1
@@ -419,27 +429,39 @@ __global__ void __launch_bounds__(256) gdfs_fp4_kernel(GemmArgs g) {
         for (int j = 0; j < 4; ++j) {
           const uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
           if (cb >= kInf || emax[i][j] == kNone) continue;  // sticky Inf/NaN; every term zero keeps c
-          c[i][j] = fixed_to_fp32(total[i][j], emax[i][j], g.F, g.rne, true);
+          c[i][j] = fixed_to_fp32(total[i][j], emax[i][j], g.F, RNE, true);
         }
     } else {
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
-          if (cb >= kInf) continue;  // sticky Inf/NaN
-          // c + acc * 2**(min es_a + min es_b - srad - 2), exact in fp64.
-          const int e2 = min_ea[i] + min_eb[j] - g.srad2;
-          const double p2 = __hiloint2double(min_ea[i] < kBig && min_eb[j] < kBig ? (e2 + 1023) << 20 : 0, 0);
+          // c + acc * 2**(min es_a + min es_b - srad - 2), exact in fp64 (the clamp only matters for an
+          // all-zero row or column, whose acc is 0).
+          const int e2 = min(max(min_ea[i] + min_eb[j] - g.srad2, -1000), 1000);
+          const double p2 = __hiloint2double((e2 + 1023) << 20, 0);
           const double v = __fma_rn((double)acc[i][j], p2, (double)c[i][j]);
-          float r = (g.rne && fabs(v) >= 0x1p-126) ? __double2float_rn(v) : __double2float_rz(v);
-          if (fabs(v) >= 0x1p128) r = v > 0 ? INFINITY : -INFINITY;
-          c[i][j] = r;
+          float r = (RNE && fabs(v) >= 0x1p-126) ? __double2float_rn(v) : __double2float_rz(v);
+          r = fabs(v) >= 0x1p128 ? __int_as_float((int)((f2u(r) & 0x80000000u) | kInf)) : r;
+          c[i][j] = (f2u(c[i][j]) & 0x7FFFFFFFu) >= kInf ? c[i][j] : r;  // Inf / NaN running value is sticky
         }
     }
-    __syncthreads();  // everyone is done with stage s
-    if (threadIdx.x == 0 && t + kStages < g.ntiles) issue(t + kStages, s);
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[s]);
+    if (threadIdx.x == 0 && producer_ok && t >= 1 && t - 1 + kStages < g.ntiles) {
+      const int sp = (int)((t - 1) % kStages);
+      if (mbar_wait(&empty[sp], (uint32_t)(((t - 1) / kStages) & 1))) {
+        issue(t - 1 + kStages, sp);
+      } else {
+        atomicExch(g.status, 1);
+        producer_ok = false;
+      }
+    }
   }
+  if (threadIdx.x == 0)
+    for (int64_t u = t; u < issued; ++u)  // copies still in flight land before the CTA exits
+      mbar_wait(&full[u % kStages], (uint32_t)((u / kStages) & 1));
+  if (t < g.ntiles) return;  // a wait ran out: the exact kernel recomputes every output
   // Epilogue: alpha, bias, output rounding (src/tricast/reference/mma.py:376-384).
   float alpha = 1.0f;
   bool has_alpha = g.alpha_a || g.alpha_b;
@@ -518,15 +540,21 @@ size_t fast_workspace(const GemmDesc &g) {
   return w ? w : cofda_workspace(g);
 }
 
-template <int NG>
-static int launch_fp4_gemm(const fp4::GemmArgs &args, int64_t M, int64_t N, cudaStream_t s) {
+template <int NG, bool RNE>
+static int launch_fp4_gemm_r(const fp4::GemmArgs &args, int64_t M, int64_t N, cudaStream_t s) {
   size_t smem = sizeof(fp4::Stage<NG>) * fp4::kStages;
-  cudaError_t e = cudaFuncSetAttribute(fp4::gdfs_fp4_kernel<NG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e =
+      cudaFuncSetAttribute(fp4::gdfs_fp4_kernel<NG, RNE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_error(std::string("gdfs fp4: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
   dim3 grid((unsigned)((N + fp4::kTileRows - 1) / fp4::kTileRows), (unsigned)((M + fp4::kTileRows - 1) / fp4::kTileRows));
-  fp4::gdfs_fp4_kernel<NG><<<grid, 256, smem, s>>>(args);
+  fp4::gdfs_fp4_kernel<NG, RNE><<<grid, 256, smem, s>>>(args);
   count_launch();
   return TC_OK;
+}
+
+template <int NG>
+static int launch_fp4_gemm(const fp4::GemmArgs &args, int64_t M, int64_t N, cudaStream_t s) {
+  return args.rne ? launch_fp4_gemm_r<NG, true>(args, M, N, s) : launch_fp4_gemm_r<NG, false>(args, M, N, s);
 }
 
 int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s) {
