@@ -142,11 +142,8 @@ __device__ __forceinline__ Term gdfs_group(const GemmDesc &g, int64_t m, int64_t
 // only_if_flag, when given, points at the fast path's {fallback flag, timeout status} pair: the
 // exact kernel runs behind a fast kernel only if the fast kernel declined the operands or one of its
 // bounded waits gave up, so a timeout still ends in the exact result.
-__global__ void __launch_bounds__(256) gemm_generic_kernel(GemmDesc g, const int32_t *only_if_flag) {
-  if (only_if_flag && only_if_flag[0] == 0 && only_if_flag[1] == 0) return;  // the fast kernel took it
-  int64_t n = (int64_t)blockIdx.x * 16 + (threadIdx.x & 15);
-  int64_t m = (int64_t)blockIdx.y * 16 + (threadIdx.x >> 4);
-  if (m >= g.M || n >= g.N) return;
+// One output of the exact product, any algorithm (src/tricast/reference/mma.py:339-384).
+__device__ __forceinline__ void generic_output(const GemmDesc &g, int64_t m, int64_t n) {
   const int64_t K = g.K;
   float acc = 0.0f;
   if (g.alg == ALG_COFDA) {
@@ -215,6 +212,18 @@ __global__ void __launch_bounds__(256) gemm_generic_kernel(GemmDesc g, const int
     }
   }
   store_out(g, m, n, epilogue(g, m, n, acc));
+}
+
+// 16 x 16 output tiles, grid-stride, one output per thread. Behind a fast kernel the grid is small, so
+// the common case (flag clear) costs a few hundred blocks that read two words and exit.
+__global__ void __launch_bounds__(256) gemm_generic_kernel(GemmDesc g, const int32_t *only_if_flag) {
+  if (only_if_flag && only_if_flag[0] == 0 && only_if_flag[1] == 0) return;  // the fast kernel took it
+  const int64_t tiles_n = (g.N + 15) / 16, tiles = tiles_n * ((g.M + 15) / 16);
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const int64_t n = (tile % tiles_n) * 16 + (threadIdx.x & 15);
+    const int64_t m = (tile / tiles_n) * 16 + (threadIdx.x >> 4);
+    if (m < g.M && n < g.N) generic_output(g, m, n);
+  }
 }
 
 // Device-side finiteness check (int_exact operands).
@@ -315,8 +324,12 @@ int build_desc(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec
 }
 
 void launch_generic(const GemmDesc &g, const int32_t *only_if_flag, cudaStream_t s) {
-  dim3 grid((unsigned)((g.N + 15) / 16), (unsigned)((g.M + 15) / 16));
-  gemm_generic_kernel<<<grid, 256, 0, s>>>(g, only_if_flag);
+  const int64_t tiles = ((g.N + 15) / 16) * ((g.M + 15) / 16);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t cap = (int64_t)sms * 8;
+  gemm_generic_kernel<<<(unsigned)(tiles < cap ? tiles : cap), 256, 0, s>>>(g, only_if_flag);
   count_launch();
 }
 

@@ -76,6 +76,7 @@ struct EncodeArgs {
   uint32_t *s;            // scale words [ntiles * ng][rows_pad]
   int32_t *flag;          // set when the fast path cannot take this operand
   int side;               // 0: A record layout, 1: B record layout
+  int vec;                // rows start 16-byte aligned: whole groups load as vectors
 };
 
 __global__ void __launch_bounds__(256) encode_fp4_kernel(EncodeArgs e) {
@@ -91,11 +92,44 @@ __global__ void __launch_bounds__(256) encode_fp4_kernel(EncodeArgs e) {
     uint32_t c0 = 0, c1 = 0, c2 = 0;     // exponent-class masks: >= 0 (nonzero), >= 1, >= 2
     uint32_t sword = pack_scale(0, 0, 0);
     if (r < e.rows) {
+      // The group's 16 inputs: vector loads when the whole group is in range and 16-byte aligned.
+      float vin[kGS];
+      if (e.vec && k0 + kGS <= e.K) {
+        if (e.dt == TC_F32) {
+          const float4 *src = reinterpret_cast<const float4 *>(static_cast<const float *>(e.v) + r * e.K + k0);
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const float4 t4 = src[w];
+            vin[4 * w] = t4.x; vin[4 * w + 1] = t4.y; vin[4 * w + 2] = t4.z; vin[4 * w + 3] = t4.w;
+          }
+        } else {
+          const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(e.v) + r * e.K + k0);
+#pragma unroll
+          for (int w = 0; w < 2; ++w) {
+            const uint4 u4 = src[w];
+            const uint32_t uu[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              if (e.dt == TC_BF16) {
+                vin[8 * w + 2 * h] = u2f(uu[h] << 16);
+                vin[8 * w + 2 * h + 1] = u2f(uu[h] & 0xFFFF0000u);
+              } else {
+                vin[8 * w + 2 * h] = __half2float(__ushort_as_half((unsigned short)(uu[h] & 0xFFFF)));
+                vin[8 * w + 2 * h + 1] = __half2float(__ushort_as_half((unsigned short)(uu[h] >> 16)));
+              }
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kGS; ++j) vin[j] = k0 + j < e.K ? load_as_float(e.v, e.dt, r * e.K + k0 + j) : 0.0f;
+      }
+#pragma unroll
       for (int j = 0; j < kGS; ++j) {
         int64_t k = k0 + j;
         int q = 0;
         if (k < e.K) {
-          float v = load_as_float(e.v, e.dt, r * e.K + k);
+          float v = vin[j];
           float t = 2.0f * v;                 // exact for finite values
           int ti = (int)t;
           int at = ti < 0 ? -ti : ti;
@@ -591,6 +625,8 @@ int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
     e.s = reinterpret_cast<uint32_t *>(ws + p.off[side * 5 + 2]);
     e.flag = flag;
     e.side = side;
+    const int esz = o.dt == TC_F32 ? 4 : 2;
+    e.vec = ((uintptr_t)o.v % 16 == 0) && ((o.K * esz) % 16 == 0);
     int64_t work = p.ntiles * p.ng * e.rows_pad;
     int64_t blocks = (work + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;

@@ -361,6 +361,15 @@ __global__ void __launch_bounds__(256) group_kernel(const void *__restrict__ x, 
 // ------------------------------------------------------------------ tensor statistics
 // One Stat for the whole tensor, reduced with atomics into a workspace slot that the host cleared
 // to the identity (amax 0, lo 0xFFFFFFFF, hi 0, nan 0). 16-byte loads when aligned.
+template <bool AMAX_ONLY>
+__device__ __forceinline__ void tstat_add(Stat &s, float v) {
+  if (AMAX_ONLY) s.amax = max(s.amax, f2u(v) & 0x7FFFFFFFu);  // NaN bits sort above Inf: NaN-propagating
+  else stat_add(s, v);
+}
+
+// AMAX_ONLY: only the NaN-propagating amax (two-level specs and absmax / pow2 tensor scales); the
+// full statistic adds the signed range for zero points.
+template <bool AMAX_ONLY>
 __global__ void __launch_bounds__(256) tensor_stats_kernel(const void *__restrict__ x, int dt, int64_t n, int vec,
                                                            Stat *__restrict__ out) {
   Stat s;
@@ -372,7 +381,8 @@ __global__ void __launch_bounds__(256) tensor_stats_kernel(const void *__restric
     int64_t n4 = n >> 2;
     for (int64_t i = tid; i < n4; i += stride) {
       float4 v = reinterpret_cast<const float4 *>(x)[i];
-      stat_add(s, v.x); stat_add(s, v.y); stat_add(s, v.z); stat_add(s, v.w);
+      tstat_add<AMAX_ONLY>(s, v.x); tstat_add<AMAX_ONLY>(s, v.y);
+      tstat_add<AMAX_ONLY>(s, v.z); tstat_add<AMAX_ONLY>(s, v.w);
     }
     done = n4 << 2;
   } else if (vec) {
@@ -380,20 +390,26 @@ __global__ void __launch_bounds__(256) tensor_stats_kernel(const void *__restric
     for (int64_t i = tid; i < n8; i += stride) {
       uint4 u = reinterpret_cast<const uint4 *>(x)[i];
       uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
       for (int j = 0; j < 4; ++j) {
         uint16_t lo = (uint16_t)(w[j] & 0xFFFF), hi = (uint16_t)(w[j] >> 16);
         if (dt == TC_BF16) {
-          stat_add(s, __bfloat162float(__ushort_as_bfloat16(lo)));
-          stat_add(s, __bfloat162float(__ushort_as_bfloat16(hi)));
+          tstat_add<AMAX_ONLY>(s, u2f((uint32_t)lo << 16));
+          tstat_add<AMAX_ONLY>(s, u2f((uint32_t)hi << 16));
         } else {
-          stat_add(s, __half2float(__ushort_as_half(lo)));
-          stat_add(s, __half2float(__ushort_as_half(hi)));
+          tstat_add<AMAX_ONLY>(s, __half2float(__ushort_as_half(lo)));
+          tstat_add<AMAX_ONLY>(s, __half2float(__ushort_as_half(hi)));
         }
       }
     }
     done = n8 << 3;
   }
-  for (int64_t i = done + tid; i < n; i += stride) stat_add(s, load_as_float(x, dt, i));
+  for (int64_t i = done + tid; i < n; i += stride) tstat_add<AMAX_ONLY>(s, load_as_float(x, dt, i));
+  if (AMAX_ONLY) {
+    for (int m = 16; m; m >>= 1) s.amax = max(s.amax, __shfl_xor_sync(0xFFFFFFFFu, s.amax, m));
+    if ((threadIdx.x & 31) == 0) atomicMax(&out->amax, s.amax);
+    return;
+  }
   for (int m = 16; m; m >>= 1) stat_merge(s, stat_shfl(s, m));
   if ((threadIdx.x & 31) == 0) {
     atomicMax(&out->amax, s.amax);
@@ -797,7 +813,10 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
   if (need_tensor_stat) {
     cudaMemsetAsync(tstat, 0, sizeof(Stat), s);
     cudaMemsetAsync(&tstat->lo, 0xFF, sizeof(uint32_t), s);
-    tensor_stats_kernel<<<grid_for((n + 7) / 8, 256, 8), 256, 0, s>>>(x, x_dtype, n, vec, tstat);
+    if (p.zp)
+      tensor_stats_kernel<false><<<grid_for((n + 7) / 8, 256, 8), 256, 0, s>>>(x, x_dtype, n, vec, tstat);
+    else
+      tensor_stats_kernel<true><<<grid_for((n + 7) / 8, 256, 8), 256, 0, s>>>(x, x_dtype, n, vec, tstat);
     ::tc::count_launch();
   }
   if (p.two_level) {

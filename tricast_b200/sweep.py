@@ -85,16 +85,16 @@ def emulate(x: torch.Tensor, w: torch.Tensor, fmt: str) -> torch.Tensor:
         zeros = qw.zero_point.repeat_interleave(128, dim=1)[:, : w.shape[1]]
         b = Operand(qw.values.float() - zeros, IntFormat("int5", 5), qw.scale, FP16, "k", 128)
         spec = MMASpec("cofda", f_bits=23, chunk_size=32, promote_interval=128, out_format="fp32")
-        return gemm_triton(as_operand(qa), b, spec)
+        return gemm_triton(as_operand(qa, compact=True), b, spec)
     scheme, preset = {"mxfp4": ("mxfp4", "nvidia_blackwell_fp4"), "nvfp4": ("nvfp4", "nvidia_blackwell_fp4"),
                       "fp8_e4m3": ("fp8_tensor", "nvidia_hopper_fp8")}[fmt]
     qa = quantize_triton(x, SCHEMES[scheme])
     qw = quantize_triton(w, SCHEMES[scheme])
-    return gemm_triton(as_operand(qa), as_operand(qw), PRESETS[preset])
+    return gemm_triton(as_operand(qa, compact=True), as_operand(qw, compact=True), PRESETS[preset])
 
 
 def reference(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    return gemm_triton(as_operand(x), as_operand(w), MMASpec("fp64", out_format="fp32"))
+    return gemm_triton(as_operand(x, compact=True), as_operand(w, compact=True), MMASpec("fp64", out_format="fp32"))
 
 
 def shard(layers: list, world: int, rank: int) -> list:
