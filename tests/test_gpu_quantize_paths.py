@@ -181,3 +181,46 @@ def test_group_quantize_ragged_group_counts(rows, K, gs, scale_name):
         if fmt.special == "none":  # no NaN encoding: a NaN element is written as code 0
             decoded = np.where(np.isnan(vals), vals, decoded)
         assert bits_equal(decoded, vals), f"{element} codes: {first_mismatch(decoded, vals)}"
+
+
+SEARCH_SPECS = {
+    "nvfp4_4o6": lambda: __import__("tricast_b200.spec", fromlist=["SCHEMES"]).SCHEMES["nvfp4_4o6"],
+    "fp8_row_mse20": lambda: QuantSpec("fp8_e4m3", "row", scale=ScaleSpec("fp32", "mse", mse_grid=20)),
+    "fp4_block_mse8": lambda: QuantSpec("fp4_e2m1", "block", block=(32, 64), scale=ScaleSpec("ue4m3", "mse", mse_grid=8)),
+    "fp4_group_mse_sr": lambda: QuantSpec("fp4_e2m1", "group", group_size=32, rounding="sr",
+                                          scale=ScaleSpec("ue4m3", "mse", mse_grid=5)),
+    "int8_tensor_p999": lambda: QuantSpec("int8", "tensor", scale=ScaleSpec("fp32", "percentile", percentile=99.9)),
+    "fp8_group_p99": lambda: QuantSpec("fp8_e4m3", "group", group_size=32,
+                                       scale=ScaleSpec("fp32", "percentile", percentile=99.0)),
+    "fp4_row_p50_two_level": lambda: QuantSpec("fp4_e2m1", "row",
+                                               scale=ScaleSpec("ue4m3", "percentile", percentile=50.0, two_level=True)),
+}
+
+
+@pytest.mark.parametrize("name", list(SEARCH_SPECS))
+@pytest.mark.parametrize("shape", [(37, 200), (64, 512)])
+def test_mse_and_percentile_scales_vs_oracle(name, shape):
+    """MSE candidate search and percentile scales on the GPU (fused group pass and the general
+    per-domain pipeline), ragged domains and a NaN row included, against the oracle."""
+    spec = SEARCH_SPECS[name]()
+    rows, K = shape
+    if spec.granularity == "group" and K % spec.group_size:
+        K = (K // spec.group_size + 1) * spec.group_size
+    rng = np.random.default_rng(zlib.crc32(f"{name}|{rows}".encode()))
+    x = rng.standard_normal((rows, K)).astype(np.float32) * 2
+    x[:, rng.choice(K, 3, replace=False)] *= 30
+    x[3, 7] = np.nan
+    kwargs = {}
+    if str(getattr(spec.rounding, "name", spec.rounding)).lower() == "sr":
+        kwargs["noise"] = rng.integers(0, 2 ** 32, (rows, K), dtype=np.uint64).astype(np.int64)
+    want = oracle_quantize(x, spec, **kwargs)
+    got, ex = quantize_into(torch.from_numpy(x).cuda(), spec, want_dequant=True,
+                            **{k: torch.from_numpy(v).cuda() for k, v in kwargs.items()})
+    for field in ("values", "scale", "global_scale"):
+        w, v = getattr(want, field), getattr(got, field)
+        assert (w is None) == (v is None), field
+        if w is not None:
+            g = v.float().cpu().numpy()
+            assert bits_equal(g, np.asarray(w)), f"{name} {field}: {first_mismatch(g, np.asarray(w))}"
+    dq = ex.dequant.cpu().numpy()
+    assert bits_equal(dq, oracle_dequantize(want)), f"{name} dequant: {first_mismatch(dq, oracle_dequantize(want))}"

@@ -264,13 +264,15 @@ __global__ void __launch_bounds__(256) element_kernel(const void *__restrict__ x
 
 // ------------------------------------------------------------------ fused group pass
 // L = group_size / 4 lanes own one group; each lane handles 4 consecutive elements.
+// MSE specs (rt.n > 0) try every candidate scale on the group before the inactive lanes of the
+// last iteration leave, so the error sums' shuffles see the full warp.
 template <int L>
 __global__ void __launch_bounds__(256) group_kernel(const void *__restrict__ x, QParams p,
                                                     const float *__restrict__ d2p, const uint32_t *__restrict__ noise,
                                                     const uint32_t *__restrict__ scale_noise, void *__restrict__ values,
                                                     float *__restrict__ scale, float *__restrict__ zero,
                                                     uint8_t *__restrict__ codes, uint8_t *__restrict__ scodes,
-                                                    float *__restrict__ dequant) {
+                                                    float *__restrict__ dequant, const Ratios rt) {
   const int64_t n = p.rows * p.K;
   const int64_t ngroups = n / (4 * L);
   const float d2 = p.two_level ? *d2p : 1.0f;
@@ -303,10 +305,30 @@ __global__ void __launch_bounds__(256) group_kernel(const void *__restrict__ x, 
     if (active)
       for (int j = 0; j < 4; ++j) stat_add(s, v[j]);
     for (int m = 1; m < L; m <<= 1) stat_merge(s, stat_shfl(s, m));
+    const uint32_t sn = (active && scale_noise) ? scale_noise[g] : 0u;
+    uint32_t nn[4] = {0u, 0u, 0u, 0u};
+    if (noise && active)
+      for (int j = 0; j < 4; ++j) nn[j] = noise[i0 + j];
+    float sc = 0.0f, z = 0.0f;
+    if (rt.n > 0) {
+      // Candidates in order; a later one wins only with a strictly smaller error (ties keep the first).
+      double best = 0.0;
+      for (int c = 0; c < rt.n; ++c) {
+        const float cs = amax_scale(__fmul_rn(u2f(s.amax), rt.r[c]), d2, p.two_level, p, sn);
+        const Divisor cdv = make_divisor(cs, d2, p.two_level, p);
+        double e = 0.0;
+        if (active)
+          for (int j = 0; j < 4; ++j) e = __dadd_rn(e, cand_sq_error(v[j], cs, cdv, d2, p.two_level, p, nn[j]));
+        for (int m = 1; m < L; m <<= 1) e = __dadd_rn(e, __shfl_xor_sync(0xFFFFFFFFu, e, m));
+        if (c == 0 || e < best) {
+          best = e;
+          sc = cs;
+        }
+      }
+    }
     if (!active) continue;  // only in the last iteration; no shuffle follows
-    uint32_t sn = scale_noise ? scale_noise[g] : 0u;
-    float sc, z = 0.0f;
-    if (p.zp) {
+    if (rt.n > 0) {
+    } else if (p.zp) {
       float lo = s.nan ? u2f(kQNaN) : unkey(s.lo);
       float hi = s.nan ? u2f(kQNaN) : unkey(s.hi);
       zp_scale(lo, hi, p, sn, sc, z);
@@ -320,9 +342,6 @@ __global__ void __launch_bounds__(256) group_kernel(const void *__restrict__ x, 
       if (p.zp) zero[g] = z;
       if (scodes) scodes[g] = (uint8_t)scale_code(sc, p.sf);
     }
-    uint32_t nn[4] = {0u, 0u, 0u, 0u};
-    if (noise)
-      for (int j = 0; j < 4; ++j) nn[j] = noise[i0 + j];
     float q[4], dq[4];
     uint32_t cd[4];
     const Divisor dv = make_divisor(sc, d2, p.two_level, p);
@@ -408,14 +427,14 @@ __global__ void __launch_bounds__(256) tensor_stats_kernel(const void *__restric
   if (AMAX_ONLY) {
     for (int m = 16; m; m >>= 1) s.amax = max(s.amax, __shfl_xor_sync(0xFFFFFFFFu, s.amax, m));
     if ((threadIdx.x & 31) == 0) atomicMax(&out->amax, s.amax);
-    return;
-  }
-  for (int m = 16; m; m >>= 1) stat_merge(s, stat_shfl(s, m));
-  if ((threadIdx.x & 31) == 0) {
-    atomicMax(&out->amax, s.amax);
-    atomicMin(&out->lo, s.lo);
-    atomicMax(&out->hi, s.hi);
-    if (s.nan) atomicExch(&out->nan, 1u);
+  } else {
+    for (int m = 16; m; m >>= 1) stat_merge(s, stat_shfl(s, m));
+    if ((threadIdx.x & 31) == 0) {
+      atomicMax(&out->amax, s.amax);
+      atomicMin(&out->lo, s.lo);
+      atomicMax(&out->hi, s.hi);
+      if (s.nan) atomicExch(&out->nan, 1u);
+    }
   }
 }
 
@@ -586,6 +605,166 @@ static void launch_flat(int grid, cudaStream_t s, const void *x, const QParams &
   }
 }
 
+// ------------------------------------------------------------------ MSE and percentile scales
+// Sum over a 256-thread block in a fixed order: butterflies within each warp, then the eight warp
+// sums in index order by thread 0 (valid in thread 0 only).
+__device__ __forceinline__ double block_sum_fixed(double v, double *warp_sums) {
+  for (int m = 16; m; m >>= 1) v = __dadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, m));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) warp_sums[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t = __dadd_rn(t, warp_sums[w]);
+  return t;
+}
+
+// Per-domain amax (NaN-propagating) from the statistic partials, one warp per domain.
+__global__ void domain_amax_kernel(int64_t nd, int parts, const Stat *__restrict__ partial, float *__restrict__ amax) {
+  const int lane = threadIdx.x & 31;
+  const int64_t d = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (d >= nd) return;
+  uint32_t a = 0;
+  for (int i = lane; i < parts; i += 32) a = max(a, partial[d * parts + i].amax);
+  for (int m = 16; m; m >>= 1) a = max(a, __shfl_xor_sync(0xFFFFFFFFu, a, m));
+  if (lane == 0) amax[d] = u2f(a);
+}
+
+// MSE search, pass 1 (src/tricast/reference/quantize.py:286-301): one block per (domain, part); for
+// every candidate ratio r the scale absmax_scale(RN(amax * r)) and the part's sum of squared errors
+// of the elements quantized and restored with it (fp64, element noise reused for every candidate).
+__global__ void __launch_bounds__(256) mse_partial_kernel(const void *__restrict__ x, QParams p, int64_t nd, int parts,
+                                                          int64_t chunk, const float *__restrict__ amax,
+                                                          const float *__restrict__ d2p,
+                                                          const uint32_t *__restrict__ noise,
+                                                          const uint32_t *__restrict__ scale_noise, const Ratios rt,
+                                                          double *__restrict__ err) {
+  __shared__ double warp_sums[8];
+  const int64_t d = blockIdx.x / parts;
+  const int part = blockIdx.x % parts;
+  if (d >= nd) return;
+  int64_t r0, c0, h, w;
+  domain_rect(p, d, r0, c0, h, w);
+  const int64_t n = h * w;
+  const int64_t beg = part * chunk, end = min(n, beg + chunk);
+  const float d2 = p.two_level ? *d2p : 1.0f;
+  const uint32_t sn = scale_noise ? scale_noise[d] : 0u;
+  for (int c = 0; c < rt.n; ++c) {
+    const float cs = amax_scale(__fmul_rn(amax[d], rt.r[c]), d2, p.two_level, p, sn);
+    const Divisor dv = make_divisor(cs, d2, p.two_level, p);
+    double e = 0.0;
+    for (int64_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
+      const int64_t idx = (r0 + i / w) * p.K + c0 + i % w;
+      e = __dadd_rn(e, cand_sq_error(load_as_float(x, p.x_dtype, idx), cs, dv, d2, p.two_level, p,
+                                     noise ? noise[idx] : 0u));
+    }
+    const double t = block_sum_fixed(e, warp_sums);
+    if (threadIdx.x == 0) err[(d * parts + part) * rt.n + c] = t;
+  }
+}
+
+// MSE search, pass 2: per domain, each candidate's error summed over the parts in order; a later
+// candidate replaces the best only with a strictly smaller error (ties keep the first).
+__global__ void mse_select_kernel(QParams p, int64_t nd, int parts, const Ratios rt, const float *__restrict__ amax,
+                                  const float *__restrict__ d2p, const uint32_t *__restrict__ scale_noise,
+                                  const double *__restrict__ err, float *__restrict__ scale,
+                                  uint8_t *__restrict__ scodes) {
+  const int64_t d = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= nd) return;
+  const float d2 = p.two_level ? *d2p : 1.0f;
+  const uint32_t sn = scale_noise ? scale_noise[d] : 0u;
+  double best = 0.0;
+  int pick = 0;
+  for (int c = 0; c < rt.n; ++c) {
+    double e = 0.0;
+    for (int part = 0; part < parts; ++part) e = __dadd_rn(e, err[(d * parts + part) * rt.n + c]);
+    if (c == 0 || e < best) {
+      best = e;
+      pick = c;
+    }
+  }
+  const float sc = amax_scale(__fmul_rn(amax[d], rt.r[pick]), d2, p.two_level, p, sn);
+  scale[d] = sc;
+  if (scodes) scodes[d] = (uint8_t)scale_code(sc, p.sf);
+}
+
+// The order statistic of rank r (0-based, ascending) among the |x| bit patterns of a domain: radix
+// select over four 8-bit digits, most significant first (non-negative floats order like their bits).
+__device__ uint32_t domain_select(const void *x, const QParams &p, int64_t r0, int64_t c0, int64_t w, int64_t n,
+                                  int64_t r, unsigned *hist, uint32_t *s_prefix, long long *s_rank) {
+  uint32_t prefix = 0, mask = 0;
+  long long rr = r;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint32_t key = f2u(load_as_float(x, p.x_dtype, (r0 + i / w) * p.K + c0 + i % w)) & 0x7FFFFFFFu;
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xFFu], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      long long cum = 0;
+      for (int b = 0; b < 256; ++b) {
+        if (cum + hist[b] > rr) {
+          *s_prefix = prefix | ((uint32_t)b << shift);
+          *s_rank = rr - cum;
+          break;
+        }
+        cum += hist[b];
+      }
+    }
+    __syncthreads();
+    prefix = *s_prefix;
+    rr = *s_rank;
+    mask |= 0xFFu << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// Percentile scale (src/tricast/reference/quantize.py:233-241, 282-283): per domain the linear
+// quantile of |x| at rank (n - 1) * percentile / 100 between the two neighbouring order statistics
+// (torch.lerp's two-sided form in fp64, then one rounding to fp32), NaN if the domain holds a NaN;
+// the scale is the absmax scale of that value. One block per domain.
+__global__ void __launch_bounds__(256) percentile_kernel(const void *__restrict__ x, QParams p, int64_t nd, double pct,
+                                                         const float *__restrict__ d2p,
+                                                         const uint32_t *__restrict__ scale_noise,
+                                                         float *__restrict__ scale, uint8_t *__restrict__ scodes) {
+  __shared__ unsigned hist[256];
+  __shared__ uint32_t s_prefix;
+  __shared__ long long s_rank;
+  for (int64_t d = blockIdx.x; d < nd; d += gridDim.x) {
+    int64_t r0, c0, h, w;
+    domain_rect(p, d, r0, c0, h, w);
+    const int64_t n = h * w;
+    int nan = 0;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
+      nan |= (f2u(load_as_float(x, p.x_dtype, (r0 + i / w) * p.K + c0 + i % w)) & 0x7FFFFFFFu) > kInf;
+    float value;
+    if (__syncthreads_or(nan)) {
+      value = u2f(kQNaN);
+    } else {
+      const double rank = __dmul_rn((double)(n - 1), pct);
+      const int64_t below = (int64_t)floor(rank), above = (int64_t)ceil(rank);
+      const double lo = (double)u2f(domain_select(x, p, r0, c0, w, n, below, hist, &s_prefix, &s_rank));
+      const double hi = (double)u2f(domain_select(x, p, r0, c0, w, n, above, hist, &s_prefix, &s_rank));
+      const double wt = __dsub_rn(rank, (double)below);
+      const double diff = __dsub_rn(hi, lo);
+      const double v = wt < 0.5 ? __dadd_rn(lo, __dmul_rn(wt, diff)) : __dsub_rn(hi, __dmul_rn(diff, __dsub_rn(1.0, wt)));
+      value = __double2float_rn(v);
+    }
+    if (threadIdx.x == 0) {
+      const float d2 = p.two_level ? *d2p : 1.0f;
+      const float sc = amax_scale(value, d2, p.two_level, p, scale_noise ? scale_noise[d] : 0u);
+      scale[d] = sc;
+      if (scodes) scodes[d] = (uint8_t)scale_code(sc, p.sf);
+    }
+    __syncthreads();
+  }
+}
+
 // ------------------------------------------------------------------ host side
 static int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
@@ -601,10 +780,13 @@ struct Plan {
   QParams p;
   Lean ln;
   LeanPow2 lp;
+  Ratios rt;          // MSE candidates (rt.n == 0: no search)
+  double pct;         // percentile / 100 (percentile method)
   int64_t nd;
   int parts;          // per-domain partials of the general path
   int path;
   size_t ws_stats, total;  // general-path partials; plus one tensor Stat slot
+  size_t off_amax, off_err;  // MSE / percentile: per-domain amax, per-(domain, part, candidate) errors
 };
 
 static int make_plan(const void *x, int32_t x_dtype, int64_t rows, int64_t K, const tc_quant_spec *spec,
@@ -674,8 +856,19 @@ static int make_plan(const void *x, int32_t x_dtype, int64_t rows, int64_t K, co
     if (sbits > 8) return set_error("scale codes need a scale format of at most 8 bits"), TC_INVALID_ARGUMENT;
     p.scode = 1;
   }
-  if (spec->scale_method == M_MSE || spec->scale_method == M_PERCENTILE)
-    return set_error("mse / percentile scale selection is not implemented by this build"), TC_UNSUPPORTED;
+  if (spec->scale_method == M_MSE) {
+    if (spec->n_search < 1 || !spec->mse_search)
+      return set_error("mse scale selection needs its candidate ratios (n_search >= 1)"), TC_INVALID_ARGUMENT;
+    if (spec->n_search > kMaxRatios)
+      return set_error("mse scale selection supports at most 256 candidates"), TC_UNSUPPORTED;
+    pl.rt.n = spec->n_search;
+    for (int c = 0; c < spec->n_search; ++c) pl.rt.r[c] = spec->mse_search[c];
+  }
+  if (spec->scale_method == M_PERCENTILE) {
+    if (!(spec->percentile > 0.0f && spec->percentile <= 100.0f))
+      return set_error("percentile must be in (0, 100]"), TC_INVALID_ARGUMENT;
+    pl.pct = (double)spec->percentile / 100.0;
+  }
   switch (spec->granularity) {
     case GRAN_TENSOR: p.dr = rows; p.dc = K; break;
     case GRAN_ROW: p.dr = 1; p.dc = K; break;
@@ -705,7 +898,9 @@ static int make_plan(const void *x, int32_t x_dtype, int64_t rows, int64_t K, co
   // The lean group pass: float elements with a nearest-even or directed rounding, no zero point,
   // 8 elements per lane (group sizes 8..128), absmax or power-of-two scales.
   const bool pow2_method = !p.two_level && (p.method == M_POW2_FLOOR || p.method == M_POW2_CEIL);
-  bool lean_ok = group_ok && pl.ln.ok && !p.zp && gs % 8 == 0 && (p.two_level || p.method == M_ABSMAX || pow2_method) &&
+  const bool searched = p.method == M_MSE || p.method == M_PERCENTILE;
+  bool lean_ok = group_ok && !searched && pl.ln.ok && !p.zp && gs % 8 == 0 &&
+                 (p.two_level || p.method == M_ABSMAX || pow2_method) &&
                  (!out->codes || ((uintptr_t)out->codes % (p.code_bits == 4 ? 8 : 16)) == 0);
   if (pow2_method) {
     float mx = (float)p.max_elem_d;
@@ -721,13 +916,21 @@ static int make_plan(const void *x, int32_t x_dtype, int64_t rows, int64_t K, co
               p.sf.emax <= 127 && (mb >> 23) != 0;
   }
   if (lean_ok) pl.path = PATH_GROUP_LEAN;
-  else if (group_ok) pl.path = PATH_GROUP;
+  else if (group_ok && p.method != M_PERCENTILE) pl.path = PATH_GROUP;  // MSE searches inside the group pass
+  else if (searched) pl.path = PATH_GENERAL;
   else if (p.dr == 1 && p.dc == K && (!out->codes || p.code_bits == 8 || K % 2 == 0)) pl.path = PATH_ROW;
   else if (p.nr == 1 && p.nc == 1) pl.path = PATH_TENSOR;
   else pl.path = PATH_GENERAL;
   pl.parts = stats_parts(p.dr * p.dc);
   pl.ws_stats = pl.path == PATH_GENERAL ? sizeof(Stat) * (size_t)pl.nd * pl.parts : 0;
-  pl.total = ((pl.ws_stats + 255) & ~(size_t)255) + 256;  // + tensor Stat slot
+  size_t off = ((pl.ws_stats + 255) & ~(size_t)255) + 256;  // + tensor Stat slot
+  if (pl.path == PATH_GENERAL && searched) {
+    pl.off_amax = off;
+    off += ((size_t)pl.nd * sizeof(float) + 255) & ~(size_t)255;
+    pl.off_err = off;
+    off += ((size_t)pl.nd * pl.parts * (size_t)(pl.rt.n > 0 ? pl.rt.n : 0) * sizeof(double) + 255) & ~(size_t)255;
+  }
+  pl.total = off;
   return TC_OK;
 }
 
@@ -775,7 +978,12 @@ extern "C" size_t tc_quantize_workspace(int64_t rows, int64_t K, const tc_quant_
   static float probe[4] __attribute__((aligned(16)));
   if (make_plan(probe, TC_F32, rows, K, spec, &dummy, pl) != TC_OK) return 256;
   size_t stats = pl.nd ? sizeof(Stat) * (size_t)pl.nd * pl.parts : 0;
-  return ((stats + 255) & ~(size_t)255) + 256;
+  size_t total = ((stats + 255) & ~(size_t)255) + 256;
+  if (spec->has_scale && (spec->scale_method == M_MSE || spec->scale_method == M_PERCENTILE)) {
+    total += ((size_t)pl.nd * sizeof(float) + 255) & ~(size_t)255;
+    total += ((size_t)pl.nd * pl.parts * (size_t)pl.rt.n * sizeof(double) + 255) & ~(size_t)255;
+  }
+  return total;
 }
 
 extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t K, const tc_quant_spec *spec,
@@ -784,6 +992,12 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
   if (!x || !spec || !out) return set_error("tc_quantize: null argument"), TC_INVALID_ARGUMENT;
   if (!out->values && !out->codes && !out->dequant)
     return set_error("tc_quantize: no element output (values, codes or dequant)"), TC_INVALID_ARGUMENT;
+  // An amax override replaces the statistic, so MSE and percentile specs search nothing: TriCast uses
+  // the absmax scale of the override (src/tricast/reference/quantize.py:282-285).
+  tc_quant_spec eff = *spec;
+  if (amax && spec->has_scale && (spec->scale_method == M_MSE || spec->scale_method == M_PERCENTILE))
+    eff.scale_method = M_ABSMAX;
+  spec = &eff;
   Plan pl;
   int st = make_plan(x, x_dtype, rows, K, spec, out, pl);
   if (st) return st;
@@ -881,12 +1095,14 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
       }
       if (done < n) {
         const LeanArgs r = shifted(done, n - done);
+        Ratios no_search;
+        no_search.n = 0;
         const int L = gs / 4;
         const int tgrid = grid_for((n - done) / gs * L, 256, 16);
 #define TC_TAIL_CASE(LL)                                                                                   \
   case LL:                                                                                                 \
     group_kernel<LL><<<tgrid, 256, 0, s>>>(r.x, r.p, d2, nullptr, r.scale_noise, r.values, r.scale, nullptr, \
-                                           r.codes, r.scodes, r.dequant);                                  \
+                                           r.codes, r.scodes, r.dequant, no_search);                       \
     break;
         switch (L) {
           TC_TAIL_CASE(2)
@@ -908,7 +1124,7 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
 #define TC_GROUP_CASE(LL)                                                                                         \
   case LL:                                                                                                        \
     group_kernel<LL><<<grid, 256, 0, s>>>(x, p, d2, noise, scale_noise, out->values, out->scale, out->zero_point, \
-                                          out->codes, out->scale_codes, out->dequant);                            \
+                                          out->codes, out->scale_codes, out->dequant, pl.rt);                     \
     ::tc::count_launch();                                                                                         \
     break;
     switch (L) {
@@ -939,11 +1155,30 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
     return launch_status("tc_quantize tensor pass");
   }
   int64_t chunk = cdiv(p.dr * p.dc, pl.parts);
-  stats_kernel<<<(unsigned)(pl.nd * pl.parts), 256, 0, s>>>(x, p, pl.nd, pl.parts, chunk, stats);
-  ::tc::count_launch();
-  scale_kernel<<<(unsigned)cdiv(pl.nd * 32, 256), 256, 0, s>>>(p, pl.nd, pl.parts, stats, nullptr, d2, scale_noise,
-                                                              out->scale, out->zero_point, out->scale_codes, 0);
-  ::tc::count_launch();
+  if (p.method == M_PERCENTILE) {
+    const int grid = (int)std::min<int64_t>(pl.nd, (int64_t)sm_count() * 8);
+    percentile_kernel<<<grid, 256, 0, s>>>(x, p, pl.nd, pl.pct, d2, scale_noise, out->scale, out->scale_codes);
+    ::tc::count_launch();
+  } else {
+    stats_kernel<<<(unsigned)(pl.nd * pl.parts), 256, 0, s>>>(x, p, pl.nd, pl.parts, chunk, stats);
+    ::tc::count_launch();
+    if (pl.rt.n > 0) {
+      float *dom_amax = reinterpret_cast<float *>(ws + pl.off_amax);
+      double *err = reinterpret_cast<double *>(ws + pl.off_err);
+      domain_amax_kernel<<<(unsigned)cdiv(pl.nd * 32, 256), 256, 0, s>>>(pl.nd, pl.parts, stats, dom_amax);
+      ::tc::count_launch();
+      mse_partial_kernel<<<(unsigned)(pl.nd * pl.parts), 256, 0, s>>>(x, p, pl.nd, pl.parts, chunk, dom_amax, d2, noise,
+                                                                      scale_noise, pl.rt, err);
+      ::tc::count_launch();
+      mse_select_kernel<<<(unsigned)cdiv(pl.nd, 256), 256, 0, s>>>(p, pl.nd, pl.parts, pl.rt, dom_amax, d2,
+                                                                  scale_noise, err, out->scale, out->scale_codes);
+      ::tc::count_launch();
+    } else {
+      scale_kernel<<<(unsigned)cdiv(pl.nd * 32, 256), 256, 0, s>>>(p, pl.nd, pl.parts, stats, nullptr, d2, scale_noise,
+                                                                  out->scale, out->zero_point, out->scale_codes, 0);
+      ::tc::count_launch();
+    }
+  }
   if ((st = launch_status("tc_quantize scales"))) return st;
   element_kernel<<<grid_for((n + 1) / 2, 256), 256, 0, s>>>(x, p, out->scale, out->zero_point, d2, noise, out->values,
                                                            out->codes, out->dequant);

@@ -226,9 +226,30 @@ __device__ __forceinline__ ElemOut quant_elem_d(float x, float s, float z, const
   return o;
 }
 
+// ------------------------------------------------------------------ MSE scale search
+// Candidate ratios of an MSE search (src/tricast/reference/quantize.py:286-301): the spec's search
+// list or linspace(1.0, 0.5, mse_grid), both as fp32, computed by the caller exactly as TriCast does.
+constexpr int kMaxRatios = 256;
+struct Ratios {
+  int n;
+  float r[kMaxRatios];
+};
+
+// Squared error of one element quantized with candidate scale s (the divisor dv of s): the
+// reference's (x - restored)**2 with restored = (q * s) [* d2], differences and squares in fp64.
+__device__ __forceinline__ double cand_sq_error(float x, float s, const Divisor &dv, float d2, bool has_d2,
+                                                const QParams &p, uint32_t noise);
+
 __device__ __forceinline__ ElemOut quant_elem(float x, float s, float z, float d2, bool has_d2, const QParams &p,
                                               uint32_t noise) {
   return quant_elem_d(x, s, z, make_divisor(s, d2, has_d2, p), d2, has_d2, p, noise);
+}
+
+__device__ __forceinline__ double cand_sq_error(float x, float s, const Divisor &dv, float d2, bool has_d2,
+                                                const QParams &p, uint32_t noise) {
+  const ElemOut o = quant_elem_d(x, s, 0.0f, dv, d2, has_d2, p, noise);
+  const double d = __dsub_rn((double)x, (double)o.dequant);
+  return __dmul_rn(d, d);
 }
 
 }  // namespace tc

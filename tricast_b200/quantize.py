@@ -9,6 +9,8 @@ device; nothing here computes values on the host.
 
 from __future__ import annotations
 
+import ctypes as C
+
 from dataclasses import dataclass
 
 import torch
@@ -96,6 +98,13 @@ def _qspec(spec) -> N.TcQuantSpec:
         s.scale_rounding = N.rounding_code(sf.rounding)
         s.two_level = int(bool(sf.two_level))
         s.percentile = float(sf.percentile)
+        if sf.method == "mse":
+            # The candidate ratios exactly as TriCast forms them (src/tricast/reference/quantize.py:290-291).
+            search = tuple(getattr(sf, "search", ()) or ())
+            ratios = (torch.tensor(search, dtype=torch.float32).tolist() if search else
+                      torch.linspace(1.0, 0.5, int(sf.mse_grid), dtype=torch.float32, device="cpu").tolist())
+            s.n_search = len(ratios)
+            s.mse_search = (C.c_float * len(ratios))(*ratios)  # kept alive by the structure
     return s
 
 
@@ -137,6 +146,9 @@ def quantize_into(x: torch.Tensor, spec, *, amax=None, noise=None, seed: int = 0
         if spec.granularity != "tensor" or amax.numel() != 1:
             raise ValueError("amax override requires tensor granularity and a scalar")
         amax = amax.to(device=device, dtype=torch.float32).reshape(()).contiguous()
+    if (N.rounding_code(spec.rounding) == 5 and noise is None and spec.scale is not None
+            and spec.scale.method == "mse"):
+        raise ValueError("MSE with stochastic rounding requires explicit noise")
     if N.rounding_code(spec.rounding) == 5 and noise is None:
         # TriCast's public API refuses SR without noise; the backend itself draws seeded noise.
         gen = torch.Generator(device=device)
