@@ -216,6 +216,7 @@ def test_fp4_single_pass_and_exact_fallback(case):
 @pytest.mark.parametrize("preset,scheme", [
     ("nvidia_hopper_fp8", "fp8_tensor"), ("nvidia_ada_fp8", "fp8_tensor"), ("nvidia_hopper_fp8", "mxfp8_e4m3"),
     ("deepseek_fp8_promote128", "fp8_group128"), ("nvidia_hopper_fp8", "mxfp8_e5m2"),
+    ("nvidia_blackwell_fp8", "fp8_tensor"), ("nvidia_blackwell_fp8", "mxfp8_e4m3"),
 ])
 def test_cofda_fast_path_vs_oracle(shape, preset, scheme):
     """The fast CoFDA kernel (epilogue, pow2 product and promoted scales) on ragged shapes."""
@@ -225,6 +226,18 @@ def test_cofda_fast_path_vs_oracle(shape, preset, scheme):
     a = _quantized(scheme, m, k, 21, outliers=min(3, k))
     b = _quantized(scheme, n, k, 22, scale=0.02)
     for spec in (PRESETS[preset].with_(out_format="fp32"), PRESETS[preset].with_(norm_rounding="rne", f_bits=9)):
+        got = gemm_triton(a, b, spec).float().cpu().numpy()
+        want = _oracle_gemm(a, b, spec)
+        assert bits_equal(got, want), f"{spec}: {first_mismatch(got, want)}"
+
+
+def test_cofda_wide_radix_fp64_path():
+    """Radices beyond fp32's exact range (F + 2 + log2(CS + 1) > 24) take the fp64 CoFDA kernel."""
+    a = _quantized("fp8_tensor", 70, 700, 41, outliers=5)
+    b = _quantized("fp8_tensor", 45, 700, 42, scale=0.02)
+    for spec in (MMASpec("cofda", f_bits=25, chunk_size=32, out_format="fp32"),
+                 MMASpec("cofda", f_bits=40, chunk_size=8, out_format="fp32", norm_rounding="rne"),
+                 MMASpec("cofda", f_bits=30, chunk_size=16, out_format="bf16")):
         got = gemm_triton(a, b, spec).float().cpu().numpy()
         want = _oracle_gemm(a, b, spec)
         assert bits_equal(got, want), f"{spec}: {first_mismatch(got, want)}"

@@ -18,6 +18,10 @@
 // This moves the per-product alignment onto the FMA pipe; the integer ALU pipe only carries the
 // sign-magic LOP3 and the packed exponent max.
 //
+// Radices up to F + 2 + log2(CS + 1) <= 53 (nvidia_blackwell_fp8, F = 25) run the same kernel in fp64:
+// operands staged as doubles, t = fma.rz(P, S, copysign(2**52, P)) - copysign(2**52, P), the running
+// value's term floor(|c| * 2**(F - emax)) by the same truncation, and exact fp64 partial sums.
+//
 // Supported here: c_mode fused, scale_apply epilogue (tensor / row scales, alpha), product with
 // power-of-two K scales (folded into the operands at encode time) and promote (per-interval
 // restart, then fp32 FMA with the interval's K scales). Anything else, and any operand or scale the
@@ -47,7 +51,7 @@ struct EncodeArgs {
   int kd;
   Fmt sf;
   int field0;
-  float *val;          // [tile][chunk][k][kTile]
+  void *val;           // [tile][chunk][k][kTile], float or double
   uint32_t *exp;       // A: [tile][chunk][k][kTile/2] (pairs of rows); B: [tile][chunk][k][kTile] (duplicated)
   int side;
   int32_t *flag;
@@ -70,6 +74,7 @@ __device__ __forceinline__ bool decode_elem(float v, const Fmt &f, int &e) {
   return true;
 }
 
+template <class T>
 __global__ void __launch_bounds__(256) encode_kernel(EncodeArgs e) {
   const int64_t pairs = e.rows_pad / 2;
   const int64_t total = pairs * e.nchunks * e.CS;
@@ -113,8 +118,8 @@ __global__ void __launch_bounds__(256) encode_kernel(EncodeArgs e) {
       exps[h] = ex;
     }
     const int64_t base = ((tile * e.nchunks + chunk) * e.CS + kk) * kTile;
-    e.val[base + rp * 2] = vals[0];
-    e.val[base + rp * 2 + 1] = vals[1];
+    static_cast<T *>(e.val)[base + rp * 2] = (T)vals[0];
+    static_cast<T *>(e.val)[base + rp * 2 + 1] = (T)vals[1];
     if (e.side == 0) {
       e.exp[base / 2 + rp] = ((uint32_t)exps[0] & 0xFFFFu) | ((uint32_t)exps[1] << 16);
     } else {
@@ -126,7 +131,7 @@ __global__ void __launch_bounds__(256) encode_kernel(EncodeArgs e) {
 }
 
 struct Args {
-  const float *av, *bv;
+  const void *av, *bv;           // staged operand values (float or double)
   const uint32_t *ae, *be;
   int64_t M, N, nchunks, a_tiles_rows, b_tiles_rows;
   int F, PI_chunks;             // chunks per promote interval (0: no promotion)
@@ -138,10 +143,10 @@ struct Args {
   int32_t *status;
 };
 
-template <int CS>
+template <int CS, class T>
 struct Stage {
-  float av[CS][kTile];
-  float bv[CS][kTile];
+  T av[CS][kTile];
+  T bv[CS][kTile];
   uint32_t be[CS][kTile];
   uint32_t ae[CS][kTile / 2];
 };
@@ -183,18 +188,64 @@ __device__ __forceinline__ float trunc_scaled(float x, float s) {
   return __fadd_rn(__fmaf_rz(x, s, m), -m);
 }
 
-template <int CS, bool RNE>
+// The accumulator arithmetic of one precision: powers of two, truncation of a scaled product and
+// the running value's term. fp32 serves F + 2 + log2(CS + 1) <= 24, fp64 up to 53.
+template <class T>
+struct Acc;
+
+template <>
+struct Acc<float> {
+  static __device__ __forceinline__ float pow2(int e) { return pow2f(e > 127 ? 127 : (e < -126 ? -126 : e)); }
+  static __device__ __forceinline__ float trunc(float x, float s) { return trunc_scaled(x, s); }
+  static __device__ __forceinline__ float mul(float a, float b) { return __fmul_rn(a, b); }
+  static __device__ __forceinline__ float add(float a, float b) { return __fadd_rn(a, b); }
+  static __device__ __forceinline__ float running(float c, int F, int emax, float) { return running_term(c, F, emax); }
+};
+
+template <>
+struct Acc<double> {
+  static __device__ __forceinline__ double pow2(int e) {
+    e = e > 1023 ? 1023 : (e < -1022 ? -1022 : e);
+    return __hiloint2double((e + 1023) << 20, 0);
+  }
+  // floor(|x| * s) with x's sign, exact for |x * s| < 2**52: fma.rz into the binade of 2**52.
+  static __device__ __forceinline__ double trunc(double x, double s) {
+    const double m = __hiloint2double((int)(((uint32_t)__double2hiint(x) & 0x80000000u) | 0x43300000u), 0);
+    return __dadd_rn(__fma_rz(x, s, m), -m);
+  }
+  static __device__ __forceinline__ double mul(double a, double b) { return __dmul_rn(a, b); }
+  static __device__ __forceinline__ double add(double a, double b) { return __dadd_rn(a, b); }
+  // floor(|c| * 2**(F - emax)) with c's sign; |c| < 2**(emax + 1), so the product is below 2**(F + 1).
+  static __device__ __forceinline__ double running(float c, int, int, double s) {
+    const uint32_t a = f2u(c) & 0x7FFFFFFFu;
+    return (a == 0 || a >= kInf) ? 0.0 : trunc((double)c, s);
+  }
+};
+
+template <class T>
+__device__ __forceinline__ void load4(const T *src, T (&o)[4]) {
+  if (sizeof(T) == 4) {
+    const float4 v = *reinterpret_cast<const float4 *>(src);
+    o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+  } else {
+    const double2 v0 = *reinterpret_cast<const double2 *>(src), v1 = *reinterpret_cast<const double2 *>(src + 2);
+    o[0] = v0.x; o[1] = v0.y; o[2] = v1.x; o[3] = v1.y;
+  }
+}
+
+template <int CS, bool RNE, class T>
 __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
   if (*p.flag) return;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  Stage<CS> *stages = reinterpret_cast<Stage<CS> *>(smem_raw);
+  Stage<CS, T> *stages = reinterpret_cast<Stage<CS, T> *>(smem_raw);
   __shared__ __align__(8) uint64_t full[kStages];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int64_t mt = blockIdx.y, nt = blockIdx.x;
   const int64_t m0 = mt * kTile, n0 = nt * kTile;
-  constexpr uint32_t kValBytes = CS * kTile * 4;
+  constexpr uint32_t kValBytes = CS * kTile * sizeof(T);
+  constexpr uint32_t kBexpBytes = CS * kTile * 4;
   constexpr uint32_t kAexpBytes = CS * (kTile / 2) * 4;
-  constexpr uint32_t kStageBytes = 3 * kValBytes + kAexpBytes;
+  constexpr uint32_t kStageBytes = 2 * kValBytes + kBexpBytes + kAexpBytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
@@ -202,14 +253,14 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
   }
   __syncthreads();
   auto issue = [&](int64_t c, int s) {
-    Stage<CS> &st = stages[s];
+    Stage<CS, T> &st = stages[s];
     mbar_expect_tx(&full[s], kStageBytes);
     const int64_t a_off = (mt * p.nchunks + c) * CS * kTile;
     const int64_t b_off = (nt * p.nchunks + c) * CS * kTile;
-    bulk_g2s(&st.av[0][0], p.av + a_off, kValBytes, &full[s]);
+    bulk_g2s(&st.av[0][0], static_cast<const T *>(p.av) + a_off, kValBytes, &full[s]);
     bulk_g2s(&st.ae[0][0], p.ae + a_off / 2, kAexpBytes, &full[s]);
-    bulk_g2s(&st.bv[0][0], p.bv + b_off, kValBytes, &full[s]);
-    bulk_g2s(&st.be[0][0], p.be + b_off, kValBytes, &full[s]);
+    bulk_g2s(&st.bv[0][0], static_cast<const T *>(p.bv) + b_off, kValBytes, &full[s]);
+    bulk_g2s(&st.be[0][0], p.be + b_off, kBexpBytes, &full[s]);
   };
   if (threadIdx.x == 0)
     for (int s = 0; s < kStages && s < p.nchunks; ++s) issue(s, s);
@@ -229,7 +280,7 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
       if (threadIdx.x == 0) atomicExch(p.status, 1);
       return;
     }
-    const Stage<CS> &st = stages[s];
+    const Stage<CS, T> &st = stages[s];
     // Pass 1: emax over two rows at once (16-bit halves).
     uint32_t em2[2][4];
 #pragma unroll
@@ -249,29 +300,27 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
       }
     }
     int emax[4][4];
-    float S[4][4], tot[4][4];
+    T S[4][4], tot[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t w = em2[i >> 1][j];
         emax[i][j] = (int)(int16_t)((i & 1) ? (w >> 16) : (w & 0xFFFFu));
-        int se = F - emax[i][j];
-        se = se > 127 ? 127 : (se < -126 ? -126 : se);
-        S[i][j] = pow2f(se);
-        tot[i][j] = running_term(c[i][j], F, emax[i][j]);
+        S[i][j] = Acc<T>::pow2(F - emax[i][j]);
+        tot[i][j] = Acc<T>::running(c[i][j], F, emax[i][j], S[i][j]);
       }
     // Pass 2: exact aligned sum.
 #pragma unroll 4
     for (int kk = 0; kk < CS; ++kk) {
-      const float4 a = *reinterpret_cast<const float4 *>(&st.av[kk][ty * 4]);
-      const float4 b = *reinterpret_cast<const float4 *>(&st.bv[kk][tx * 4]);
-      const float as[4] = {a.x, a.y, a.z, a.w};
-      const float bs[4] = {b.x, b.y, b.z, b.w};
+      T as[4], bs[4];
+      load4<T>(&st.av[kk][ty * 4], as);
+      load4<T>(&st.bv[kk][tx * 4], bs);
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) tot[i][j] = __fadd_rn(tot[i][j], trunc_scaled(__fmul_rn(as[i], bs[j]), S[i][j]));
+        for (int j = 0; j < 4; ++j)
+          tot[i][j] = Acc<T>::add(tot[i][j], Acc<T>::trunc(Acc<T>::mul(as[i], bs[j]), S[i][j]));
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i)
@@ -279,8 +328,8 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
       for (int j = 0; j < 4; ++j) {
         const uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
         if (cb >= kInf) continue;  // an overflowed running value is sticky (operands are finite)
-        const int32_t t = (int32_t)tot[i][j];
-        c[i][j] = t == 0 ? 0.0f : fixed_to_fp32_i32(t, emax[i][j], F, RNE);
+        const int64_t t = (int64_t)tot[i][j];
+        c[i][j] = t == 0 ? 0.0f : fixed_to_fp32(t, emax[i][j], F, RNE, true);
       }
     if (p.PI_chunks && (ch + 1) % p.PI_chunks == 0 || p.PI_chunks && ch + 1 == p.nchunks) {
       // End of a promote interval: acc = fma(partial, (1 * sa) * sb, acc), partial restarts at 0.
@@ -314,7 +363,7 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
 
 // ---------------------------------------------------------------- dispatch
 struct CofdaPlan {
-  bool ok;
+  bool ok, wide;
   int CS;
   int64_t nchunks, a_pad, b_pad;
   size_t off[4], total, flag_off;
@@ -330,7 +379,8 @@ static CofdaPlan plan_cofda(const GemmDesc &g) {
   if (!narrow_float(g.a.f) || !narrow_float(g.b.f)) return p;
   int width_bits = 0;
   while ((1 << width_bits) <= g.CS) ++width_bits;  // bit length of CS (covers CS + 1 terms)
-  if (g.F + 2 + width_bits > 24) return p;
+  if (g.F + 2 + width_bits > 53) return p;
+  p.wide = g.F + 2 + width_bits > 24;  // fp64 accumulation
   if (g.apply == AP_PRODUCT) {
     for (const OpDesc *o : {&g.a, &g.b})
       if (o->skind == SK_K && o->sf.kind != 2) return p;  // only power-of-two product scales fold
@@ -345,7 +395,8 @@ static CofdaPlan plan_cofda(const GemmDesc &g) {
   p.a_pad = (g.M + cofda::kTile - 1) / cofda::kTile * cofda::kTile;
   p.b_pad = (g.N + cofda::kTile - 1) / cofda::kTile * cofda::kTile;
   const size_t ka = (size_t)p.a_pad * p.nchunks * g.CS, kb = (size_t)p.b_pad * p.nchunks * g.CS;
-  size_t sizes[4] = {ka * 4, ka * 2, kb * 4, kb * 4};
+  const size_t vsz = p.wide ? 8 : 4;
+  size_t sizes[4] = {ka * vsz, ka * 2, kb * vsz, kb * 4};
   size_t off = 0;
   for (int i = 0; i < 4; ++i) {
     p.off[i] = off;
@@ -362,16 +413,21 @@ size_t cofda_workspace(const GemmDesc &g) {
   return p.ok ? p.total : 0;
 }
 
-template <int CS, bool RNE>
-static int launch_cofda_kernel(const cofda::Args &a, cudaStream_t s) {
-  size_t smem = sizeof(cofda::Stage<CS>) * cofda::kStages;
-  cudaError_t e = cudaFuncSetAttribute(cofda::cofda_kernel<CS, RNE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+template <int CS, bool RNE, class T>
+static int launch_cofda_kernel_t(const cofda::Args &a, cudaStream_t s) {
+  size_t smem = sizeof(cofda::Stage<CS, T>) * cofda::kStages;
+  cudaError_t e = cudaFuncSetAttribute(cofda::cofda_kernel<CS, RNE, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return set_error(std::string("cofda: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
   dim3 grid((unsigned)((a.N + cofda::kTile - 1) / cofda::kTile), (unsigned)((a.M + cofda::kTile - 1) / cofda::kTile));
-  cofda::cofda_kernel<CS, RNE><<<grid, 256, smem, s>>>(a);
+  cofda::cofda_kernel<CS, RNE, T><<<grid, 256, smem, s>>>(a);
   count_launch();
   return TC_OK;
+}
+
+template <int CS, bool RNE>
+static int launch_cofda_kernel(const cofda::Args &a, bool wide, cudaStream_t s) {
+  return wide ? launch_cofda_kernel_t<CS, RNE, double>(a, s) : launch_cofda_kernel_t<CS, RNE, float>(a, s);
 }
 
 int launch_cofda(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s) {
@@ -399,21 +455,22 @@ int launch_cofda(const GemmDesc &g, void *workspace, size_t workspace_bytes, cud
     e.kd = o.kd;
     e.sf = o.sf;
     e.field0 = o.field0;
-    e.val = reinterpret_cast<float *>(ws + p.off[side * 2]);
+    e.val = ws + p.off[side * 2];
     e.exp = reinterpret_cast<uint32_t *>(ws + p.off[side * 2 + 1]);
     e.side = side;
     e.flag = flag;
     int64_t work = (e.rows_pad / 2) * p.nchunks * p.CS;
     int64_t blocks = (work + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    cofda::encode_kernel<<<(unsigned)blocks, 256, 0, s>>>(e);
+    if (p.wide) cofda::encode_kernel<double><<<(unsigned)blocks, 256, 0, s>>>(e);
+    else cofda::encode_kernel<float><<<(unsigned)blocks, 256, 0, s>>>(e);
     count_launch();
   }
   cofda::Args a;
   std::memset(&a, 0, sizeof(a));
-  a.av = reinterpret_cast<const float *>(ws + p.off[0]);
+  a.av = ws + p.off[0];
   a.ae = reinterpret_cast<const uint32_t *>(ws + p.off[1]);
-  a.bv = reinterpret_cast<const float *>(ws + p.off[2]);
+  a.bv = ws + p.off[2];
   a.be = reinterpret_cast<const uint32_t *>(ws + p.off[3]);
   a.M = g.M;
   a.N = g.N;
@@ -429,9 +486,9 @@ int launch_cofda(const GemmDesc &g, void *workspace, size_t workspace_bytes, cud
   a.flag = flag;
   a.status = flag + 1;
   int st;
-  if (p.CS == 32) st = g.rne ? launch_cofda_kernel<32, true>(a, s) : launch_cofda_kernel<32, false>(a, s);
-  else if (p.CS == 16) st = g.rne ? launch_cofda_kernel<16, true>(a, s) : launch_cofda_kernel<16, false>(a, s);
-  else st = g.rne ? launch_cofda_kernel<8, true>(a, s) : launch_cofda_kernel<8, false>(a, s);
+  if (p.CS == 32) st = g.rne ? launch_cofda_kernel<32, true>(a, p.wide, s) : launch_cofda_kernel<32, false>(a, p.wide, s);
+  else if (p.CS == 16) st = g.rne ? launch_cofda_kernel<16, true>(a, p.wide, s) : launch_cofda_kernel<16, false>(a, p.wide, s);
+  else st = g.rne ? launch_cofda_kernel<8, true>(a, p.wide, s) : launch_cofda_kernel<8, false>(a, p.wide, s);
   if (st) return st;
   launch_generic(g, flag, s);
   cudaError_t e = cudaGetLastError();
