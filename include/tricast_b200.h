@@ -187,6 +187,11 @@ const char *tc_last_error(void);
 /* Number of kernels this library has launched in the process (all threads, all devices). */
 uint64_t tc_launch_count(void);
 
+/* How many times, on the current device, the exact generic GEMM kernel queued behind a fast kernel
+ * has actually run (the fast kernel declined the operands or one of its waits ran out). Waits for the
+ * device. */
+int tc_exact_fallbacks(uint64_t *count);
+
 /* Library version string. */
 const char *tc_version(void);
 

@@ -11,6 +11,7 @@ import oracle
 from tests.conftest import bits_equal, first_mismatch
 from tests.golden_cases import bf16_bits, load, mma_operand, mspec, nadpe_cases
 from tricast_b200 import gemm_triton, quantize_triton
+from tricast_b200.mma import exact_fallbacks
 from tricast_b200.formats import FP16, IntFormat
 from tricast_b200.operand import Operand, as_operand
 from tricast_b200.spec import PRESETS, SCHEMES, MMASpec
@@ -78,7 +79,9 @@ def test_preset_configs_vs_oracle(scheme, preset, out):
     a = _quantized(scheme, 64, 1024, 1, outliers=4)
     b = _quantized(scheme, 96, 1024, 2, scale=0.02)
     spec = PRESETS[preset].with_(out_format=out)
+    before = exact_fallbacks()
     got = gemm_triton(a, b, spec).float().cpu().numpy()
+    assert exact_fallbacks() == before, "the fast kernel declined benchmark-config operands"
     want = _oracle_gemm(a, b, spec)
     assert bits_equal(got, want), first_mismatch(got, want)
 
@@ -226,7 +229,9 @@ def test_cofda_fast_path_vs_oracle(shape, preset, scheme):
     a = _quantized(scheme, m, k, 21, outliers=min(3, k))
     b = _quantized(scheme, n, k, 22, scale=0.02)
     for spec in (PRESETS[preset].with_(out_format="fp32"), PRESETS[preset].with_(norm_rounding="rne", f_bits=9)):
+        before = exact_fallbacks()
         got = gemm_triton(a, b, spec).float().cpu().numpy()
+        assert exact_fallbacks() == before, f"{spec}: the fast kernel declined finite on-grid operands"
         want = _oracle_gemm(a, b, spec)
         assert bits_equal(got, want), f"{spec}: {first_mismatch(got, want)}"
 
@@ -274,3 +279,24 @@ def test_int_promote_fast_path_vs_oracle(shape):
     b8 = as_operand(quantize_triton(torch.randn(n, k, generator=g).cuda(), SCHEMES["int8_row"]))
     spec = MMASpec("int_exact", out_format="fp32")
     assert bits_equal(gemm_triton(a8, b8, spec).cpu().numpy(), _oracle_gemm(a8, b8, spec))
+
+
+@pytest.mark.parametrize("rows", [40, 3])  # tiled kernel and small-M kernel
+def test_cofda_tiny_folded_scales(rows):
+    """Power-of-two product scales that fold into tiny values: labels down to -50 stay on the fast
+    kernels (exact scale powers, a chunk of zero products with a tiny running value), lower ones go
+    to the exact kernel."""
+    a = _quantized("mxfp8_e4m3", rows, 512, 51)
+    b = _quantized("mxfp8_e4m3", 33, 512, 52, scale=0.02)
+    spec = PRESETS["nvidia_hopper_fp8"].with_(out_format="fp32")
+    for exp_a, exp_b, fast in ((-40, -3, True), (-44, -40, True), (-58, 0, False)):
+        sa = torch.full_like(a.scale, 2.0 ** exp_a)
+        sb = torch.full_like(b.scale, 2.0 ** exp_b)
+        sb[:, 3] = 2.0 ** -127  # E8M0 code 0, a zero scale: a chunk of zero products after the first
+        ta = Operand(a.values, a.fmt, sa, a.scale_fmt, a.scale_kind, a.k_domain, a.alpha)
+        tb = Operand(b.values, b.fmt, sb, b.scale_fmt, b.scale_kind, b.k_domain, b.alpha)
+        before = exact_fallbacks()
+        got = gemm_triton(ta, tb, spec).cpu().numpy()
+        assert (exact_fallbacks() == before) == fast, (exp_a, exp_b)
+        want = _oracle_gemm(ta, tb, spec)
+        assert bits_equal(got, want), f"{exp_a} {exp_b}: {first_mismatch(got, want)}"

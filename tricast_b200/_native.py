@@ -76,6 +76,7 @@ EXPORTS = {
     "tc_last_error": (C.c_char_p, []),
     "tc_version": (C.c_char_p, []),
     "tc_launch_count": (C.c_uint64, []),
+    "tc_exact_fallbacks": (C.c_int, [C.POINTER(C.c_uint64)]),
 }
 
 _lib = None

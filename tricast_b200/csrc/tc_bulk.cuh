@@ -50,4 +50,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 
 __device__ __forceinline__ void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 
+// 16 bytes global -> shared without registers (both addresses 16-byte aligned). A thread's copies
+// are complete after cp_async_wait_all; a following __syncthreads makes every thread's copies visible.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 }  // namespace tc

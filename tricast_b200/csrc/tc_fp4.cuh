@@ -1,0 +1,151 @@
+// E2M1 x E2M1 GDFS building blocks shared by the tiled kernel (tc_gemm_fast.cu) and the small-M
+// kernel (tc_gemv.cu): the operand record encoder, the scale word, exponent-class labels, DP4A group
+// dot products and the running value's FDA term.
+#pragma once
+
+#include "tc_gemm.cuh"
+
+namespace tc {
+namespace fp4 {
+
+constexpr int kGS = 16;          // GDFS group size of the fast path
+constexpr int kNone = -(1 << 28);  // "no active term" exponent
+constexpr int kBig = 1 << 28;
+
+// Scale word: es (int16, biased by 0x8000 in bits 0..15), ms (bits 16..23), sign (bit 24), the
+// group's largest exponent class (bits 25..26) and "every code of the group is zero" (bit 27).
+__host__ __device__ __forceinline__ uint32_t pack_scale(int es, uint32_t ms, uint32_t neg) {
+  return ((uint32_t)(es + 0x8000) & 0xFFFFu) | ((ms & 0xFFu) << 16) | ((neg & 1u) << 24);
+}
+
+// Doubled E2M1 codes of one group (int8 lanes of q; elements j >= valid are zero), the exponent-class
+// masks (c0: non-zero, c1: |v| >= 2, c2: |v| >= 4) and whether any value is off the E2M1 grid
+// (NaN / Inf included).
+__device__ __forceinline__ void e2m1_codes(const float (&vin)[kGS], int valid, uint4 &q, uint32_t &c0, uint32_t &c1,
+                                           uint32_t &c2, bool &bad) {
+  uint32_t codes[4] = {0, 0, 0, 0};
+  c0 = c1 = c2 = 0;
+#pragma unroll
+  for (int j = 0; j < kGS; ++j) {
+    int qv = 0;
+    if (j < valid) {
+      const float t = 2.0f * vin[j];  // exact for finite values
+      const int ti = (int)t;
+      const int at = ti < 0 ? -ti : ti;
+      const bool on_grid = (float)ti == t && (at <= 4 || at == 6 || at == 8 || at == 12);
+      if (!on_grid) bad = true;
+      qv = ti;
+      if (at) {
+        c0 |= 1u << j;
+        if (at >= 4) c1 |= 1u << j;
+        if (at >= 8) c2 |= 1u << j;
+      }
+    }
+    codes[j >> 2] |= ((uint32_t)(qv & 0xFF)) << (8 * (j & 3));
+  }
+  q = make_uint4(codes[0], codes[1], codes[2], codes[3]);
+}
+
+// The doubled E2M1 code of one container element from its bit pattern, without float <-> int
+// conversions: |v| in {0.5, 1, 1.5, 2, 3, 4, 6} sits at (bits - bits(0.5)) >> (fraction bits - 1) in
+// {0, 2, 3, 4, 5, 6, 7} with the lower fraction bits zero, and the code's magnitude is the nibble
+// of 0xC8643201 at that index (index 1 is 0.75, off the grid). Zero (either sign) is code 0. Anything
+// else (off-grid values, NaN, Inf) clears ok.
+template <int DT>
+__device__ __forceinline__ int e2m1_code_bits(uint32_t bits, bool &ok) {
+  constexpr uint32_t kAbs = DT == TC_F32 ? 0x7FFFFFFFu : 0x7FFFu;
+  constexpr int kHalf = DT == TC_F32 ? 0x3F000000 : (DT == TC_BF16 ? 0x3F00 : 0x3800);
+  constexpr int kShift = DT == TC_F32 ? 22 : (DT == TC_BF16 ? 6 : 9);
+  constexpr int kLow = (1 << kShift) - 1;
+  constexpr uint32_t kSign = DT == TC_F32 ? 0x80000000u : 0x8000u;
+  const uint32_t a = bits & kAbs;
+  const int d = (int)a - kHalf;
+  const int r = d >> kShift;
+  const bool on = a == 0u || ((d & kLow) == 0 && (unsigned)r <= 7u && r != 1);
+  ok &= on;
+  const int mag = a == 0u ? 0 : (int)((0xC8643201u >> ((4 * r) & 31)) & 0xFu);
+  return (bits & kSign) ? -mag : mag;
+}
+
+// A group's K scale as (es, ms, sign) at the scale format's radix, or zero (the group becomes a zero
+// term, mma.py:270-276). Scale significands up to 4 bits (UE4M3, E4M3, E8M0) keep
+// |D| * ms_a * ms_b < 2**20; |es| <= 400 keeps every fp64 power 2**(es_a + es_b - srad - 2) normal.
+__device__ __forceinline__ uint32_t group_scale_word(float s, const Fmt &sf, int field0, bool &zero, bool &bad) {
+  const Term t = decode_term(s, sf);
+  if (t.nan || t.inf || t.sig > 15 || t.exp < -400 || t.exp > 400) bad = true;
+  zero = t.zero || (field0 && f2u(s) == 0x00400000u);
+  return zero ? pack_scale(0, 0, 0) : pack_scale(t.exp, (uint32_t)t.sig, t.neg ? 1u : 0u);
+}
+
+struct EncodeArgs {
+  const void *v;
+  int dt;
+  int64_t rows, K, rows_pad, ntiles;
+  int ng;                 // groups per K tile
+  const float *scale;     // K scales or nullptr
+  int64_t nkd;
+  int kd;
+  Fmt sf;
+  int field0;
+  uint4 *q;               // [ntiles * ng][rows_pad]
+  uint4 *m;
+  uint32_t *s;            // scale words [ntiles * ng][rows_pad]
+  int32_t *flag;          // set when the fast path cannot take this operand
+  int side;               // 0: A record layout, 1: B record layout
+  int vec;                // rows start 16-byte aligned: whole groups load as vectors
+};
+
+// Encodes an operand into records [ntiles * ng][rows_pad] (tc_gemm_fast.cu).
+__global__ void __launch_bounds__(256) encode_fp4_kernel(EncodeArgs e);
+
+// Exponent-class masks of one group in the record layouts exp_class_max pairs up (A: side 0, B: side 1).
+__device__ __forceinline__ uint4 a_masks(uint32_t c0, uint32_t c1, uint32_t c2) {
+  return make_uint4(c0 | (c1 << 16), c2 | (c1 << 16), c2, c2);
+}
+__device__ __forceinline__ uint4 b_masks(uint32_t c0, uint32_t c1, uint32_t c2) {
+  return make_uint4(c1 | (c0 << 16), c1 | (c2 << 16), c0, c2 | (c1 << 16));
+}
+
+__device__ __forceinline__ int exp_class_max(const uint4 &a, const uint4 &b) {
+  // a = {A0|A1<<16, A2|A1<<16, A2, A2}, b = {B1|B0<<16, B1|B2<<16, B0, B2|B1<<16}
+  uint32_t t1 = a.x & b.x;                  // A0&B1 | A1&B0        (sum >= 1)
+  uint32_t t2 = (a.x & b.w) | (a.z & b.z);  // A0&B2 | A1&B1 | A2&B0 (sum >= 2)
+  uint32_t t3 = a.y & b.y;                  // A2&B1 | A1&B2        (sum >= 3)
+  uint32_t t4 = a.w & b.w;                  // A2&B2                (sum = 4; a.w has no high half)
+  return (int)(t1 != 0) + (int)(t2 != 0) + (int)(t3 != 0) + (int)(t4 != 0);
+}
+
+__device__ __forceinline__ int dot16(const uint4 &a, const uint4 &b) {
+  int d = __dp4a((int)a.x, (int)b.x, 0);
+  d = __dp4a((int)a.y, (int)b.y, d);
+  d = __dp4a((int)a.z, (int)b.z, d);
+  return __dp4a((int)a.w, (int)b.w, d);
+}
+
+__device__ __forceinline__ int scale_exp(uint32_t w) { return (int)(w & 0xFFFFu) - 0x8000; }
+
+// Exponent of the running value as an FDA term (mma.py:85-91); kNone for 0 / Inf / NaN.
+__device__ __forceinline__ int running_exp(float c) {
+  uint32_t a = f2u(c) & 0x7FFFFFFFu;
+  if (a == 0 || a >= kInf) return kNone;
+  uint32_t field = a >> 23;
+  if (field) return (int)field - 127;
+  return ilog2_u32(a) - 149;
+}
+
+// The running value's significand at radix F, aligned to emax with truncation, signed.
+__device__ __forceinline__ int64_t running_term(float c, int F, int emax) {
+  uint32_t a = f2u(c) & 0x7FFFFFFFu;
+  if (a == 0 || a >= kInf) return 0;
+  uint32_t field = a >> 23;
+  uint32_t sig = field ? ((a & 0x7FFFFFu) | 0x800000u) : a;
+  int lead = ilog2_u32(sig);
+  int ec = (field ? (int)field - 127 : -126) + lead - 23;
+  uint64_t m = (uint64_t)(sig << (23 - lead));  // 24-bit, leading one at bit 23
+  int sh = (F - 23) - (emax - ec);
+  uint64_t v = sh >= 0 ? (m << sh) : (sh <= -64 ? 0ull : (m >> -sh));
+  return (f2u(c) >> 31) ? -(int64_t)v : (int64_t)v;
+}
+
+}  // namespace fp4
+}  // namespace tc

@@ -216,8 +216,12 @@ __device__ __forceinline__ void generic_output(const GemmDesc &g, int64_t m, int
 
 // 16 x 16 output tiles, grid-stride, one output per thread. Behind a fast kernel the grid is small, so
 // the common case (flag clear) costs a few hundred blocks that read two words and exit.
+// Runs of the exact kernel behind a fast kernel that declined its operands (or timed out), per device.
+__device__ unsigned long long g_exact_fallbacks;
+
 __global__ void __launch_bounds__(256) gemm_generic_kernel(GemmDesc g, const int32_t *only_if_flag) {
   if (only_if_flag && only_if_flag[0] == 0 && only_if_flag[1] == 0) return;  // the fast kernel took it
+  if (only_if_flag && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(&g_exact_fallbacks, 1ull);
   const int64_t tiles_n = (g.N + 15) / 16, tiles = tiles_n * ((g.M + 15) / 16);
   for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
     const int64_t n = (tile % tiles_n) * 16 + (threadIdx.x & 15);
@@ -356,6 +360,15 @@ extern "C" int tc_gemm(const tc_operand *a, const tc_operand *b, const tc_mma_sp
   launch_generic(g, nullptr, s);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(std::string("tc_gemm: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
+  return TC_OK;
+}
+
+extern "C" int tc_exact_fallbacks(uint64_t *count) {
+  if (!count) return set_error("tc_exact_fallbacks: null argument"), TC_INVALID_ARGUMENT;
+  unsigned long long v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_exact_fallbacks, sizeof(v));
+  if (e != cudaSuccess) return set_error(std::string("tc_exact_fallbacks: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
+  *count = (uint64_t)v;
   return TC_OK;
 }
 

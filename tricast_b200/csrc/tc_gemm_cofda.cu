@@ -31,14 +31,13 @@
 #include <string>
 
 #include "tc_bulk.cuh"
-#include "tc_gemm.cuh"
+#include "tc_cofda.cuh"
 
 namespace tc {
 namespace cofda {
 
 constexpr int kTile = 64;     // rows of A and columns of B per CTA
 constexpr int kStages = 3;
-constexpr int kZeroExp = -8192;  // exponent label of a zero element (int16)
 
 struct EncodeArgs {
   const void *v;
@@ -56,23 +55,6 @@ struct EncodeArgs {
   int side;
   int32_t *flag;
 };
-
-__device__ __forceinline__ bool decode_elem(float v, const Fmt &f, int &e) {
-  uint32_t u = f2u(v);
-  uint32_t a = u & 0x7FFFFFFFu;
-  if (a >= kInf) return false;
-  if (a == 0) {
-    e = kZeroExp;
-    return true;
-  }
-  Term t = decode_term(v, f);
-  // On-grid check: the decoded significand must reproduce |v| exactly (mbits <= 3 here).
-  if (t.sig == 0 || t.sig >= (1ull << (f.mbits + 1))) return false;
-  float back = ldexpf((float)t.sig, t.exp - f.mbits);
-  if (back != fabsf(v)) return false;
-  e = t.exp;
-  return true;
-}
 
 template <class T>
 __global__ void __launch_bounds__(256) encode_kernel(EncodeArgs e) {
@@ -106,8 +88,9 @@ __global__ void __launch_bounds__(256) encode_kernel(EncodeArgs e) {
             v = 0.0f;
             ex = kZeroExp;
           } else {
-            // Keep every folded value inside [2**-60, 2**61) so products stay normal fp32 values.
-            if (ts.exp < -60 || ts.exp > 60 || ex + ts.exp < -60 || ex + ts.exp > 60) bad = true;
+            // Folded labels in [-50, 60]: products stay normal fp32 values, and a chunk with a non-zero
+            // product has emax >= -100, so its scale 2**(F - emax) is a normal fp32 power.
+            if (ts.exp < -60 || ts.exp > 60 || ex + ts.exp < -50 || ex + ts.exp > 60) bad = true;
             v = ldexpf(v, ts.exp);
             ex += ts.exp;
           }
@@ -150,88 +133,6 @@ struct Stage {
   uint32_t be[CS][kTile];
   uint32_t ae[CS][kTile / 2];
 };
-
-// Normalise an exact int32 fixed-point total (mma.py:118-137, FDA form).
-__device__ __forceinline__ float fixed_to_fp32_i32(int32_t total, int exponent, int radix, bool rne) {
-  return fixed_to_fp32((int64_t)total, exponent, radix, rne, true);
-}
-
-__device__ __forceinline__ int running_exp(float c) {
-  uint32_t a = f2u(c) & 0x7FFFFFFFu;
-  if (a == 0 || a >= kInf) return kZeroExp;
-  uint32_t field = a >> 23;
-  return field ? (int)field - 127 : ilog2_u32(a) - 149;
-}
-
-// The running value as an FDA term at radix F <= 23, aligned to emax with truncation: its 24-bit
-// significand shifted right by (23 - F) + (emax - ec) (mma.py:85-91 then the alignment shift).
-// Exact integer below 2**(F+1), returned as fp32.
-__device__ __forceinline__ float running_term(float c, int F, int emax) {
-  const uint32_t a = f2u(c) & 0x7FFFFFFFu;
-  if (a == 0 || a >= kInf) return 0.0f;
-  const uint32_t field = a >> 23;
-  const uint32_t sig = field ? ((a & 0x7FFFFFu) | 0x800000u) : a;
-  const int lead = ilog2_u32(sig);
-  const int ec = (field ? (int)field - 127 : -126) + lead - 23;
-  const uint32_t norm = sig << (23 - lead);
-  const int sh = (23 - F) + (emax - ec);
-  const uint32_t v = sh >= 32 ? 0u : (norm >> sh);
-  return (f2u(c) >> 31) ? -(float)v : (float)v;
-}
-
-// 2**e as fp32 for e in [-126, 127] (callers clamp).
-__device__ __forceinline__ float pow2f(int e) { return u2f((uint32_t)(e + 127) << 23); }
-
-// floor(|x| * s) with x's sign, exact for |x * s| < 2**23 (x * s exact or not).
-__device__ __forceinline__ float trunc_scaled(float x, float s) {
-  const float m = u2f((f2u(x) & 0x80000000u) | 0x4B000000u);
-  return __fadd_rn(__fmaf_rz(x, s, m), -m);
-}
-
-// The accumulator arithmetic of one precision: powers of two, truncation of a scaled product and
-// the running value's term. fp32 serves F + 2 + log2(CS + 1) <= 24, fp64 up to 53.
-template <class T>
-struct Acc;
-
-template <>
-struct Acc<float> {
-  static __device__ __forceinline__ float pow2(int e) { return pow2f(e > 127 ? 127 : (e < -126 ? -126 : e)); }
-  static __device__ __forceinline__ float trunc(float x, float s) { return trunc_scaled(x, s); }
-  static __device__ __forceinline__ float mul(float a, float b) { return __fmul_rn(a, b); }
-  static __device__ __forceinline__ float add(float a, float b) { return __fadd_rn(a, b); }
-  static __device__ __forceinline__ float running(float c, int F, int emax, float) { return running_term(c, F, emax); }
-};
-
-template <>
-struct Acc<double> {
-  static __device__ __forceinline__ double pow2(int e) {
-    e = e > 1023 ? 1023 : (e < -1022 ? -1022 : e);
-    return __hiloint2double((e + 1023) << 20, 0);
-  }
-  // floor(|x| * s) with x's sign, exact for |x * s| < 2**52: fma.rz into the binade of 2**52.
-  static __device__ __forceinline__ double trunc(double x, double s) {
-    const double m = __hiloint2double((int)(((uint32_t)__double2hiint(x) & 0x80000000u) | 0x43300000u), 0);
-    return __dadd_rn(__fma_rz(x, s, m), -m);
-  }
-  static __device__ __forceinline__ double mul(double a, double b) { return __dmul_rn(a, b); }
-  static __device__ __forceinline__ double add(double a, double b) { return __dadd_rn(a, b); }
-  // floor(|c| * 2**(F - emax)) with c's sign; |c| < 2**(emax + 1), so the product is below 2**(F + 1).
-  static __device__ __forceinline__ double running(float c, int, int, double s) {
-    const uint32_t a = f2u(c) & 0x7FFFFFFFu;
-    return (a == 0 || a >= kInf) ? 0.0 : trunc((double)c, s);
-  }
-};
-
-template <class T>
-__device__ __forceinline__ void load4(const T *src, T (&o)[4]) {
-  if (sizeof(T) == 4) {
-    const float4 v = *reinterpret_cast<const float4 *>(src);
-    o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
-  } else {
-    const double2 v0 = *reinterpret_cast<const double2 *>(src), v1 = *reinterpret_cast<const double2 *>(src + 2);
-    o[0] = v0.x; o[1] = v0.y; o[2] = v1.x; o[3] = v1.y;
-  }
-}
 
 template <int CS, bool RNE, class T>
 __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
@@ -328,8 +229,7 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
       for (int j = 0; j < 4; ++j) {
         const uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
         if (cb >= kInf) continue;  // an overflowed running value is sticky (operands are finite)
-        const int64_t t = (int64_t)tot[i][j];
-        c[i][j] = t == 0 ? 0.0f : fixed_to_fp32(t, emax[i][j], F, RNE, true);
+        c[i][j] = Acc<T>::finish(tot[i][j], emax[i][j], F, RNE);
       }
     if (p.PI_chunks && (ch + 1) % p.PI_chunks == 0 || p.PI_chunks && ch + 1 == p.nchunks) {
       // End of a promote interval: acc = fma(partial, (1 * sa) * sb, acc), partial restarts at 0.
@@ -408,9 +308,14 @@ static CofdaPlan plan_cofda(const GemmDesc &g) {
   return p;
 }
 
+bool cofda_gemv_eligible(const GemmDesc &g);
+size_t cofda_gemv_workspace(const GemmDesc &g, bool wide);
+int launch_cofda_gemv(const GemmDesc &g, bool wide, void *workspace, size_t workspace_bytes, cudaStream_t s);
+
 size_t cofda_workspace(const GemmDesc &g) {
   CofdaPlan p = plan_cofda(g);
-  return p.ok ? p.total : 0;
+  if (!p.ok) return 0;
+  return cofda_gemv_eligible(g) ? cofda_gemv_workspace(g, p.wide) : p.total;
 }
 
 template <int CS, bool RNE, class T>
@@ -433,6 +338,7 @@ static int launch_cofda_kernel(const cofda::Args &a, bool wide, cudaStream_t s) 
 int launch_cofda(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s) {
   CofdaPlan p = plan_cofda(g);
   if (!p.ok) return TC_UNSUPPORTED;
+  if (cofda_gemv_eligible(g)) return launch_cofda_gemv(g, p.wide, workspace, workspace_bytes, s);
   if (!workspace || workspace_bytes < p.total) return set_error("tc_gemm: workspace too small"), TC_WORKSPACE_TOO_SMALL;
   if ((g.M + cofda::kTile - 1) / cofda::kTile > 65535) return TC_UNSUPPORTED;
   char *ws = static_cast<char *>(workspace);

@@ -43,41 +43,14 @@
 #include <string>
 
 #include "tc_bulk.cuh"
-#include "tc_gemm.cuh"
+#include "tc_fp4.cuh"
 
 namespace tc {
 
 namespace fp4 {
 
-constexpr int kGS = 16;          // GDFS group size of the fast path
 constexpr int kTileRows = 64;    // rows (A) / columns (B) per CTA
 constexpr int kStages = 4;
-constexpr int kNone = -(1 << 28);  // "no active term" exponent
-constexpr int kBig = 1 << 28;
-
-// Scale word: es (int16, biased by 0x8000 in bits 0..15), ms (bits 16..23), sign (bit 24), the
-// group's largest exponent class (bits 25..26) and "every code of the group is zero" (bit 27).
-__host__ __device__ __forceinline__ uint32_t pack_scale(int es, uint32_t ms, uint32_t neg) {
-  return ((uint32_t)(es + 0x8000) & 0xFFFFu) | ((ms & 0xFFu) << 16) | ((neg & 1u) << 24);
-}
-
-struct EncodeArgs {
-  const void *v;
-  int dt;
-  int64_t rows, K, rows_pad, ntiles;
-  int ng;                 // groups per K tile
-  const float *scale;     // K scales or nullptr
-  int64_t nkd;
-  int kd;
-  Fmt sf;
-  int field0;
-  uint4 *q;               // [ntiles * ng][rows_pad]
-  uint4 *m;
-  uint32_t *s;            // scale words [ntiles * ng][rows_pad]
-  int32_t *flag;          // set when the fast path cannot take this operand
-  int side;               // 0: A record layout, 1: B record layout
-  int vec;                // rows start 16-byte aligned: whole groups load as vectors
-};
 
 __global__ void __launch_bounds__(256) encode_fp4_kernel(EncodeArgs e) {
   int64_t ngroups_row = e.ntiles * e.ng;
@@ -124,48 +97,19 @@ __global__ void __launch_bounds__(256) encode_fp4_kernel(EncodeArgs e) {
 #pragma unroll
         for (int j = 0; j < kGS; ++j) vin[j] = k0 + j < e.K ? load_as_float(e.v, e.dt, r * e.K + k0 + j) : 0.0f;
       }
-#pragma unroll
-      for (int j = 0; j < kGS; ++j) {
-        int64_t k = k0 + j;
-        int q = 0;
-        if (k < e.K) {
-          float v = vin[j];
-          float t = 2.0f * v;                 // exact for finite values
-          int ti = (int)t;
-          int at = ti < 0 ? -ti : ti;
-          bool on_grid = (float)ti == t && (at <= 4 || at == 6 || at == 8 || at == 12);
-          if (!on_grid) bad = true;           // also catches NaN / Inf
-          q = ti;
-          if (at) {
-            c0 |= 1u << j;
-            if (at >= 4) c1 |= 1u << j;       // |v| >= 2: exponent class 1 or 2
-            if (at >= 8) c2 |= 1u << j;       // |v| >= 4: exponent class 2
-          }
-        }
-        codes[j >> 2] |= ((uint32_t)(q & 0xFF)) << (8 * (j & 3));
-      }
-      int es = 0;
-      uint32_t ms = 1, neg = 0;
+      uint4 qq;
+      const int64_t left = e.K - k0;
+      e2m1_codes(vin, left < kGS ? (int)left : kGS, qq, c0, c1, c2, bad);
+      codes[0] = qq.x; codes[1] = qq.y; codes[2] = qq.z; codes[3] = qq.w;
       bool zero = false;
-      if (e.scale) {
-        float s = e.scale[r * e.nkd + k0 / e.kd];
-        Term t = decode_term(s, e.sf);
-        // Scale significands up to 4 bits (UE4M3, E4M3, E8M0) keep |D| * ms_a * ms_b < 2**20.
-        // |es| <= 400 keeps every fp64 power 2**(es_a + es_b - srad - 2) a normal number.
-        if (t.nan || t.inf || t.sig > 15 || t.exp < -400 || t.exp > 400) bad = true;
-        zero = t.zero || (e.field0 && f2u(s) == 0x00400000u);
-        es = t.exp;
-        ms = (uint32_t)t.sig;
-        neg = t.neg ? 1u : 0u;
-      }
+      // No K scale: es = 0, ms = 1. Groups past K (padding of the last tile) read no scale.
+      sword = (e.scale && k0 < e.K) ? group_scale_word(e.scale[r * e.nkd + k0 / e.kd], e.sf, e.field0, zero, bad)
+                                    : pack_scale(0, 1, 0);
       if (zero) {
         // A zero scale makes the whole group a zero term (the group rule of mma.py:270-276);
         // zero codes give D = 0 for every partner, so the group never enters emax.
         codes[0] = codes[1] = codes[2] = codes[3] = 0;
         c0 = c1 = c2 = 0;
-        sword = pack_scale(0, 0, 0);
-      } else {
-        sword = pack_scale(es, ms, neg);
       }
       const uint32_t gemax = c2 ? 2u : c1 ? 1u : 0u;
       sword |= (gemax << 25) | ((c0 == 0 ? 1u : 0u) << 27);
@@ -173,12 +117,7 @@ __global__ void __launch_bounds__(256) encode_fp4_kernel(EncodeArgs e) {
       sword |= 1u << 27;  // padding rows are all-zero groups
     }
     uint4 q4 = make_uint4(codes[0], codes[1], codes[2], codes[3]);
-    uint4 m4;
-    if (e.side == 0) {
-      m4 = make_uint4(c0 | (c1 << 16), c2 | (c1 << 16), c2, c2);
-    } else {
-      m4 = make_uint4(c1 | (c0 << 16), c1 | (c2 << 16), c0, c2 | (c1 << 16));
-    }
+    const uint4 m4 = e.side == 0 ? a_masks(c0, c1, c2) : b_masks(c0, c1, c2);
     e.q[idx] = q4;
     e.m[idx] = m4;
     e.s[idx] = sword;
@@ -251,47 +190,6 @@ struct Stage {
   int2 btw[kTileRows];
 };
 
-
-__device__ __forceinline__ int exp_class_max(const uint4 &a, const uint4 &b) {
-  // a = {A0|A1<<16, A2|A1<<16, A2, A2}, b = {B1|B0<<16, B1|B2<<16, B0, B2|B1<<16}
-  uint32_t t1 = a.x & b.x;                  // A0&B1 | A1&B0        (sum >= 1)
-  uint32_t t2 = (a.x & b.w) | (a.z & b.z);  // A0&B2 | A1&B1 | A2&B0 (sum >= 2)
-  uint32_t t3 = a.y & b.y;                  // A2&B1 | A1&B2        (sum >= 3)
-  uint32_t t4 = a.w & b.w;                  // A2&B2                (sum = 4; a.w has no high half)
-  return (int)(t1 != 0) + (int)(t2 != 0) + (int)(t3 != 0) + (int)(t4 != 0);
-}
-
-__device__ __forceinline__ int dot16(const uint4 &a, const uint4 &b) {
-  int d = __dp4a((int)a.x, (int)b.x, 0);
-  d = __dp4a((int)a.y, (int)b.y, d);
-  d = __dp4a((int)a.z, (int)b.z, d);
-  return __dp4a((int)a.w, (int)b.w, d);
-}
-
-__device__ __forceinline__ int scale_exp(uint32_t w) { return (int)(w & 0xFFFFu) - 0x8000; }
-
-// Exponent of the running value as an FDA term (mma.py:85-91); kNone for 0 / Inf / NaN.
-__device__ __forceinline__ int running_exp(float c) {
-  uint32_t a = f2u(c) & 0x7FFFFFFFu;
-  if (a == 0 || a >= kInf) return kNone;
-  uint32_t field = a >> 23;
-  if (field) return (int)field - 127;
-  return ilog2_u32(a) - 149;
-}
-
-// The running value's significand at radix F, aligned to emax with truncation, signed.
-__device__ __forceinline__ int64_t running_term(float c, int F, int emax) {
-  uint32_t a = f2u(c) & 0x7FFFFFFFu;
-  if (a == 0 || a >= kInf) return 0;
-  uint32_t field = a >> 23;
-  uint32_t sig = field ? ((a & 0x7FFFFFu) | 0x800000u) : a;
-  int lead = ilog2_u32(sig);
-  int ec = (field ? (int)field - 127 : -126) + lead - 23;
-  uint64_t m = (uint64_t)(sig << (23 - lead));  // 24-bit, leading one at bit 23
-  int sh = (F - 23) - (emax - ec);
-  uint64_t v = sh >= 0 ? (m << sh) : (sh <= -64 ? 0ull : (m >> -sh));
-  return (f2u(c) >> 31) ? -(int64_t)v : (int64_t)v;
-}
 
 // 256 threads as 16 x 16; thread (ty, tx) owns rows ty*4 + i and columns tx + 16*j of the tile.
 template <int NG, bool RNE>
@@ -567,9 +465,15 @@ size_t int_workspace(const GemmDesc &g);
 int launch_fma(const GemmDesc &g, cudaStream_t s);
 int launch_int(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
 
+size_t fp4_gemv_workspace(const GemmDesc &g);
+int launch_fp4_gemv(const GemmDesc &g, int ng, void *workspace, size_t workspace_bytes, cudaStream_t s);
+
+// Decode shapes (at most this many rows of A) take the small-M kernels (tc_gemv.cu).
+constexpr int64_t kGemvMaxM = 16;
+
 size_t fast_workspace(const GemmDesc &g) {
   Fp4Plan p = plan_fp4(g);
-  if (p.ok) return p.total;
+  if (p.ok) return g.M <= kGemvMaxM ? fp4_gemv_workspace(g) : p.total;
   size_t w = int_workspace(g);
   return w ? w : cofda_workspace(g);
 }
@@ -600,6 +504,7 @@ int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
     if (st != TC_UNSUPPORTED) return st;
     return launch_fma(g, s);
   }
+  if (g.M <= kGemvMaxM) return launch_fp4_gemv(g, p.ng, workspace, workspace_bytes, s);
   if (!workspace || workspace_bytes < p.total) return set_error("tc_gemm: workspace too small"), TC_WORKSPACE_TOO_SMALL;
   if (p.ntiles * fp4::kTileRows > (int64_t)1 << 40) return TC_UNSUPPORTED;
   char *ws = static_cast<char *>(workspace);

@@ -9,6 +9,8 @@ copy is made.
 
 from __future__ import annotations
 
+import ctypes as C
+
 import torch
 
 from . import _native as N
@@ -158,6 +160,17 @@ def gemm_triton(a, b, spec, bias: torch.Tensor | None = None) -> torch.Tensor:
     return out
 
 
+def exact_fallbacks(device=None) -> int:
+    """How many times, on ``device``, the exact generic kernel queued behind a fast GEMM kernel has run
+    because the fast kernel declined its operands (non-finite or off-grid values, scales it cannot
+    fold) or a bounded wait ran out. Synchronises the device."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    count = C.c_uint64(0)
+    with torch.cuda.device(device):
+        N.check(N.lib().tc_exact_fallbacks(C.byref(count)), "tc_exact_fallbacks")
+    return int(count.value)
+
+
 def gemm(a, b, spec, *, bias: torch.Tensor | None = None) -> torch.Tensor:
     """TriCast ``gemm`` on CUDA operands (``mma/api.py:63-109``): activations [..., K] × weights [N, K]."""
     from .operand import Operand, as_operand
@@ -175,4 +188,4 @@ def gemm(a, b, spec, *, bias: torch.Tensor | None = None) -> torch.Tensor:
     return out.reshape(*a_shape[:-1], b_op.rows)
 
 
-__all__ = ["gemm_triton", "gemm", "resolve_scale_apply", "check_headroom", "get_format"]
+__all__ = ["gemm_triton", "gemm", "exact_fallbacks", "resolve_scale_apply", "check_headroom", "get_format"]
