@@ -67,6 +67,41 @@ __device__ __forceinline__ int e2m1_code_bits(uint32_t bits, bool &ok) {
   return (bits & kSign) ? -mag : mag;
 }
 
+// PTX prmt in its default mode: result byte k is byte c[k] & 7 of {b, a}, sign-replicated when bit 3 of
+// the selector nibble is set.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Doubled E2M1 codes of four bf16 container values (w0 holds elements 0 and 1, element 0 in the low
+// half; w1 elements 2 and 3) as int8 lanes, four at a time:
+//   * bits 8..6 of a bf16 E2M1 value (the exponent's low bit and the top two fraction bits) index
+//     its magnitude: 2.0, 3.0, 4.0, 6.0, 0.5, 0.75, 1.0, 1.5 for indices 0..7, so one byte permute
+//     of a table gives the four |2v| (0.75 is off the grid and maps to 0);
+//   * zero elements (+-0) are masked out through bit 15 of each half of (|w| + 0x7FFF);
+//   * the grid check rebuilds each magnitude's bf16 pattern from its code and compares it with the
+//     input, which rejects everything else (other fraction bits, other exponents, NaN, Inf, 0.75);
+//   * signs become byte masks by sign-replicating permutes, and a negative code is (m ^ 0xFF) + 1
+//     per byte (no carry: m >= 1 where the mask is set).
+// orm collects the magnitudes: bit 3 of a byte marks |v| >= 4, bits 2..3 |v| >= 2.
+__device__ __forceinline__ uint32_t e2m1_codes4_bf16(uint32_t w0, uint32_t w1, bool &ok, uint32_t &orm) {
+  const uint32_t x0 = w0 & 0x7FFF7FFFu, x1 = w1 & 0x7FFF7FFFu;
+  const uint32_t nz = prmt(x0 + 0x7FFF7FFFu, x1 + 0x7FFF7FFFu, 0xFDB9u);
+  const uint32_t t0 = (w0 >> 6) & 0x00070007u, t1 = (w1 >> 6) & 0x00070007u;
+  const uint32_t sel = ((t0 | (t0 >> 12)) & 0xFFu) | (((t1 | (t1 >> 12)) & 0xFFu) << 8);
+  const uint32_t mag = prmt(0x0C080604u, 0x03020001u, sel) & nz;
+  const uint32_t live8 = mag + 0x7F7F7F7Fu;  // bit 7 of byte k: element k has a code
+  const uint32_t lo = prmt(0xC0804000u, 0xC0804000u, sel), hi = prmt(0x40404040u, 0x3F3F3F3Fu, sel);
+  const uint32_t r0 = prmt(lo, hi, 0x5140u) & prmt(live8, live8, 0x9988u);
+  const uint32_t r1 = prmt(lo, hi, 0x7362u) & prmt(live8, live8, 0xBBAAu);
+  ok &= (r0 == x0) & (r1 == x1);
+  const uint32_t smask = prmt(w0, w1, 0xFDB9u) & prmt(live8, live8, 0xBA98u);
+  orm |= mag;
+  return (mag ^ smask) + (smask & 0x01010101u);
+}
+
 // A group's K scale as (es, ms, sign) at the scale format's radix, or zero (the group becomes a zero
 // term, mma.py:270-276). Scale significands up to 4 bits (UE4M3, E4M3, E8M0) keep
 // |D| * ms_a * ms_b < 2**20; |es| <= 400 keeps every fp64 power 2**(es_a + es_b - srad - 2) normal.
@@ -75,6 +110,26 @@ __device__ __forceinline__ uint32_t group_scale_word(float s, const Fmt &sf, int
   if (t.nan || t.inf || t.sig > 15 || t.exp < -400 || t.exp > 400) bad = true;
   zero = t.zero || (field0 && f2u(s) == 0x00400000u);
   return zero ? pack_scale(0, 0, 0) : pack_scale(t.exp, (uint32_t)t.sig, t.neg ? 1u : 0u);
+}
+
+// group_scale_word for a normal fp32 scale value of a float or power-of-two scale format, on the bit
+// pattern (decode_term's exponent max(floor log2 |s|, emin) and truncated significand at the format's
+// radix); zero, subnormal and non-finite scales and integer scale formats take group_scale_word.
+__device__ __forceinline__ uint32_t group_scale_word_fast(float s, const Fmt &sf, int field0, bool &zero, bool &bad) {
+  const uint32_t u = f2u(s), a = u & 0x7FFFFFFFu, field = a >> 23;
+  if (field == 0u || field == 255u || sf.kind == 1) return group_scale_word(s, sf, field0, zero, bad);
+  zero = false;
+  const int fl = (int)field - 127;
+  int e = fl;
+  uint32_t sig = 1;
+  if (sf.kind == 0) {
+    e = fl > sf.emin ? fl : sf.emin;
+    const int r = 23 - sf.mbits + e - fl;
+    sig = r >= 24 ? 0u : (((a & 0x7FFFFFu) | 0x800000u) >> r);
+    if (sig == 0u) e = 0;
+  }
+  if (sig > 15u) bad = true;  // |e| <= 127 here
+  return pack_scale(e, sig, u >> 31);
 }
 
 struct EncodeArgs {

@@ -465,7 +465,7 @@ size_t int_workspace(const GemmDesc &g);
 int launch_fma(const GemmDesc &g, cudaStream_t s);
 int launch_int(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
 
-size_t fp4_gemv_workspace(const GemmDesc &g);
+size_t fp4_gemv_workspace(const GemmDesc &g, int ng);
 int launch_fp4_gemv(const GemmDesc &g, int ng, void *workspace, size_t workspace_bytes, cudaStream_t s);
 
 // Decode shapes (at most this many rows of A) take the small-M kernels (tc_gemv.cu).
@@ -473,7 +473,7 @@ constexpr int64_t kGemvMaxM = 16;
 
 size_t fast_workspace(const GemmDesc &g) {
   Fp4Plan p = plan_fp4(g);
-  if (p.ok) return g.M <= kGemvMaxM ? fp4_gemv_workspace(g) : p.total;
+  if (p.ok) return g.M <= kGemvMaxM ? fp4_gemv_workspace(g, p.ng) : p.total;
   size_t w = int_workspace(g);
   return w ? w : cofda_workspace(g);
 }

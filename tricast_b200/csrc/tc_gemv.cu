@@ -33,15 +33,24 @@
 
 #include "tc_bulk.cuh"
 #include "tc_fp4.cuh"
+#include "tc_generic.cuh"
 
 namespace tc {
 namespace gemv {
 
 constexpr int kThreads = 256;
-constexpr int kCols = 16;                  // columns (rows of B) per CTA
-constexpr int kGroups = 32;                // groups per chunk: one per lane
-constexpr int kDCol = kCols + 1;           // padded column stride of the product table (words)
-constexpr int kDRow = kGroups * kDCol + 16;  // padded row stride: rows m and m + 1 hit other banks
+constexpr int kGroups = 32;  // groups per chunk: one per lane
+
+// Per (column, K tile, row of A): the tile's value over its groups with D != 0 (exact when their
+// exponent spread is at most 30), the largest label bound and the smallest scale exponent sum.
+struct TileRec {
+  double sum;
+  int lmax, emin;
+};
+
+// Slabs whose small-M kernels fell back to the exact routine, per device (reported with the generic
+// kernel's count by tc_exact_fallbacks).
+__device__ unsigned long long g_gemv_fallbacks;
 
 struct Fp4Args {
   const uint4 *aq, *am;      // A records [groups][mp] (codes, exponent-class masks), padded to whole chunks
@@ -59,6 +68,10 @@ struct Fp4Args {
   Fmt of;
   int out_plain, out_dt;
   void *out;
+  GemmDesc g;                // the whole product, for the exact fallback
+  int64_t ngroups_pad;       // groups rounded up to whole chunks
+  TileRec *rec;              // [ns][ntiles][M]
+  int64_t ntiles, n_base, ns;  // K tiles; the slab of columns [n_base, n_base + ns)
   int32_t *flag;             // nonzero: the fast path cannot take the operands
 };
 
@@ -144,8 +157,16 @@ __device__ __forceinline__ void b_group_fast(const Fp4Args &p, int64_t n, int64_
   uint32_t codes[4] = {0, 0, 0, 0};
   int maxmag = 0;
   bool ok = true;
+  if (DT == TC_BF16) {
+    uint32_t orm = 0;
+    codes[0] = fp4::e2m1_codes4_bf16(r.u[0].x, r.u[0].y, ok, orm);
+    codes[1] = fp4::e2m1_codes4_bf16(r.u[0].z, r.u[0].w, ok, orm);
+    codes[2] = fp4::e2m1_codes4_bf16(r.u[1].x, r.u[1].y, ok, orm);
+    codes[3] = fp4::e2m1_codes4_bf16(r.u[1].z, r.u[1].w, ok, orm);
+    maxmag = (orm & 0x08080808u) ? 8 : (orm & 0x0C0C0C0Cu) ? 4 : (orm ? 1 : 0);
+  }
 #pragma unroll
-  for (int j = 0; j < fp4::kGS; ++j) {
+  for (int j = 0; j < (DT == TC_BF16 ? 0 : fp4::kGS); ++j) {
     uint32_t bits;
     if (DT == TC_F32) {
       const uint4 &u = r.u[j >> 2];
@@ -162,7 +183,7 @@ __device__ __forceinline__ void b_group_fast(const Fp4Args &p, int64_t n, int64_
   }
   if (!ok) bad = true;
   bool zero = false;
-  sword = p.bscale ? fp4::group_scale_word(p.bscale[n * p.b_nkd + k0 / p.b_kd], p.bsf, p.b_field0, zero, bad)
+  sword = p.bscale ? fp4::group_scale_word_fast(p.bscale[n * p.b_nkd + k0 / p.b_kd], p.bsf, p.b_field0, zero, bad)
                    : fp4::pack_scale(0, 1, 0);
   if (zero) {
     codes[0] = codes[1] = codes[2] = codes[3] = 0;
@@ -176,157 +197,170 @@ __device__ __forceinline__ void b_group_fast(const Fp4Args &p, int64_t n, int64_
 
 __device__ __forceinline__ double pow2d(int e) { return __hiloint2double((e + 1023) << 20, 0); }
 
-template <int DT, bool RNE>
-__global__ void __launch_bounds__(kThreads) gdfs_fp4_gemv_kernel(Fp4Args p) {
-  if (*p.flag) return;  // A could not be encoded: the generic kernel takes over
-  // Dynamic shared memory: products D [2][M][kDRow] (int32), then A's records of three chunks (a ring:
-  // codes [3][kGroups * mp] uint4, scale words [3][kGroups * mp] uint32).
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ uint32_t bsw[2][kGroups][kDCol];  // B scale words of the chunk
-  const int M = (int)p.M, mp = p.mp;
-  int32_t *dsm = reinterpret_cast<int32_t *>(smem_raw);
-  uint4 *saq = reinterpret_cast<uint4 *>(smem_raw + (size_t)2 * M * kDRow * sizeof(int32_t));
-  uint32_t *sas = reinterpret_cast<uint32_t *>(saq + 3 * kGroups * mp);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t n0 = (int64_t)blockIdx.x * kCols;
-  const int64_t nchunks = (p.ngroups + kGroups - 1) / kGroups;
-  // Scan role: thread (m, col) for m < M.
-  const int sm = threadIdx.x / kCols, scol = threadIdx.x % kCols;
-  const bool scanner = sm < M;
-  const int64_t sn = n0 + scol;
-  float c = 0.0f;
-  bool bad = false;
+// Phase 1. CTA = two chunks of 32 groups (lane = group) x 8 columns (warp = column). Each lane decodes
+// its B groups from the container, forms D against every row of A (the chunks' A records staged in
+// shared memory) and each group's value and bounds; lanes of a K tile combine them with xor shuffles
+// and the tile's first lane writes the record.
+constexpr int kChunksPerCta = 2;
 
-  // A's records of one chunk (contiguous: the arrays are padded to whole chunks) into a ring slot.
-  auto copy_a = [&](int64_t ch) {
-    const int slot = (int)(ch % 3);
-    const int nq = kGroups * mp, ns = kGroups * mp / 4;
-    for (int i = threadIdx.x; i < nq + ns; i += kThreads) {
-      if (i < nq) cp_async16(saq + slot * nq + i, p.aq + ch * nq + i);
-      else cp_async16(sas + slot * nq + 4 * (i - nq), p.as + ch * nq + 4 * (i - nq));
-    }
+template <int DT>
+__global__ void __launch_bounds__(kThreads) gdfs_fp4_tiles_kernel(Fp4Args p) {
+  if (*p.flag) return;  // A could not be encoded: the scan kernel computes every output exactly
+  __shared__ uint4 saq[kChunksPerCta][kGroups * 16];
+  __shared__ uint32_t sas[kChunksPerCta][kGroups * 16];
+  const int mp = p.mp, M = (int)p.M, ng = p.ng;
+  const int64_t nchunks = p.ngroups_pad / kGroups;
+  const int64_t ch0 = (int64_t)blockIdx.x * kChunksPerCta;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t col = (int64_t)blockIdx.y * 8 + warp;  // column within the slab
+  const int64_t n = p.n_base + col;
+  const int nc = (int)(nchunks - ch0 < kChunksPerCta ? nchunks - ch0 : kChunksPerCta);
+  {
+    const int nq = kGroups * mp, ns = nq / 4;
+    for (int c = 0; c < nc; ++c)
+      for (int i = threadIdx.x; i < nq + ns; i += kThreads) {
+        if (i < nq) cp_async16(&saq[c][i], p.aq + (ch0 + c) * nq + i);
+        else cp_async16(&sas[c][4 * (i - nq)], p.as + (ch0 + c) * nq + 4 * (i - nq));
+      }
     cp_async_commit();
-  };
-  copy_a(0);
-  Raw<DT> raw[2];
-  raw_load<DT>(p, n0 + warp, lane, raw[0]);
-  raw_load<DT>(p, n0 + warp + 8, lane, raw[1]);
+  }
+  uint4 bq[kChunksPerCta];
+  uint32_t swb[kChunksPerCta];
+  bool bad = false;
+  {
+    Raw<DT> r[kChunksPerCta];
+#pragma unroll
+    for (int c = 0; c < kChunksPerCta; ++c) raw_load<DT>(p, n, (ch0 + c) * kGroups + lane, r[c]);
+#pragma unroll
+    for (int c = 0; c < kChunksPerCta; ++c) {
+      const int64_t gi = (ch0 + c) * kGroups + lane;
+      bq[c] = make_uint4(0, 0, 0, 0);
+      swb[c] = fp4::pack_scale(0, 0, 0) | (1u << 27);
+      if (col < p.ns && n < p.N && gi < p.ngroups) b_group_fast<DT>(p, n, gi, r[c], bq[c], swb[c], bad);
+    }
+  }
   cp_async_wait_all();
   __syncthreads();
-  for (int64_t ch = 0; ch < nchunks; ++ch) {
-    const int buf = (int)(ch & 1), slot = (int)(ch % 3);
-    if (ch + 1 < nchunks) copy_a(ch + 1);  // lands during this chunk; the ring slot was last read two chunks ago
-    const int64_t gi = ch * kGroups + lane;
-    int32_t *dbuf = dsm + buf * M * kDRow;
-    // Encode this lane's group of both columns and form D against every row of A.
-    uint4 bq[2];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int col = warp + 8 * j;
-      const int64_t n = n0 + col;
-      uint32_t sword = fp4::pack_scale(0, 0, 0) | (1u << 27);
-      bq[j] = make_uint4(0, 0, 0, 0);
-      if (n < p.N && gi < p.ngroups) b_group_fast<DT>(p, n, gi, raw[j], bq[j], sword, bad);
-      bsw[buf][lane][col] = sword;
-    }
-    // Next chunk's raw values are in flight while this one is multiplied and scanned.
-    if (ch + 1 < nchunks) {
-      raw_load<DT>(p, n0 + warp, gi + kGroups, raw[0]);
-      raw_load<DT>(p, n0 + warp + 8, gi + kGroups, raw[1]);
-    }
-    const uint4 *arow = saq + slot * kGroups * mp + lane * mp;
+  for (int c = 0; c < kChunksPerCta; ++c) {
+    if (c >= nc) break;
+    const int64_t tile = ((ch0 + c) * kGroups + lane) / ng;
+    const bool writer = (lane % ng) == 0 && col < p.ns && n < p.N && tile < p.ntiles;
+    const int eb = fp4::scale_exp(swb[c]), cb = (int)((swb[c] >> 25) & 3u);
+    const uint32_t msb = (swb[c] >> 16) & 0xFFu;
     for (int m = 0; m < M; ++m) {
-      const uint4 aq = arow[m];  // zero codes past K (the encoder pads)
-      dbuf[m * kDRow + lane * kDCol + warp] = fp4::dot16(aq, bq[0]);
-      dbuf[m * kDRow + lane * kDCol + warp + 8] = fp4::dot16(aq, bq[1]);
-    }
-    cp_async_wait_all();
-    __syncthreads();
-    if (scanner && sn < p.N) {
-      const int32_t *drow = dbuf + sm * kDRow;
-      const uint32_t *swa_row = sas + slot * kGroups * mp + sm;
-      const int ng = p.ng, tiles = kGroups / ng;
-      for (int t = 0; t < tiles; ++t) {
-        const int64_t g0 = ch * kGroups + t * ng;
-        if (g0 >= p.ngroups) break;
-        const uint32_t cb = f2u(c) & 0x7FFFFFFFu;
-        if (cb >= kInf) break;  // an Inf / NaN running value is sticky
-        int d[8];
-        uint32_t swa[8], swb[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          if (q < ng) {
-            const int l = t * ng + q;
-            d[q] = drow[l * kDCol + scol];
-            swa[q] = swa_row[l * mp];
-            swb[q] = bsw[buf][l][scol];
-          } else {
-            d[q] = 0;
-            swa[q] = swb[q] = 0;
-          }
-        }
-        // Bounds and fp64 value of the tile over its groups with D != 0.
-        double sum = 0.0;
-        int lmax = fp4::kNone, emin = fp4::kBig;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int e = fp4::scale_exp(swa[q]) + fp4::scale_exp(swb[q]);
-          const int x = d[q] * (int)(((swa[q] >> 16) & 0xFFu) * ((swb[q] >> 16) & 0xFFu));
-          const bool neg = ((swa[q] ^ swb[q]) >> 24) & 1u;
-          if (d[q] != 0) {
-            lmax = max(lmax, e + (int)((swa[q] >> 25) & 3u) + (int)((swb[q] >> 25) & 3u));
-            emin = min(emin, e);
-            sum = __fma_rn((double)(neg ? -x : x), pow2d(e - p.srad2), sum);
-          }
-        }
-        if (lmax == fp4::kNone) continue;  // every group sum is zero: the tile leaves c as it is
-        const int be = (int)(cb >> 23);
-        const int lo = max(lmax - (p.F - 23) + 127, 1);
-        const int hi = emin + p.F - p.srad2 + 127;
-        const bool safe = lmax - emin <= 30 && lmax <= emin - p.srad2 + p.F && (cb == 0 || (be >= lo && be <= hi));
-        if (safe) {
-          const double v = __dadd_rn(sum, (double)c);  // exact: both are multiples of 2**(emax'' - F), |v| < 2**(emax'' + 4)
-          float r = (RNE && fabs(v) >= 0x1p-126) ? __double2float_rn(v) : __double2float_rz(v);
-          c = fabs(v) >= 0x1p128 ? __int_as_float((int)((f2u(r) & 0x80000000u) | kInf)) : r;
-          continue;
-        }
-        // Exact two-pass step (mma.py:318-336): exponent labels from the exponent-class masks (A's
-        // from its records, B's recomputed from the raw group), then the aligned, truncated integer
-        // terms and the fixed-point normalisation. Rare; the operands are read again from shared memory.
-        int emax = fp4::running_exp(c);
-        for (int q = 0; q < ng; ++q) {
-          const int l = t * ng + q;
-          if (drow[l * kDCol + scol] == 0) continue;
-          Raw<DT> rr;
-          raw_load<DT>(p, sn, g0 + q, rr);
-          uint4 q4, bm;
-          uint32_t sw;
-          bool ignored = false;
-          b_group<DT>(p, sn, g0 + q, rr, q4, sw, bm, ignored);
-          const int label = fp4::exp_class_max(__ldg(p.am + (g0 + q) * mp + sm), bm) + fp4::scale_exp(swa_row[l * mp]) +
-                            fp4::scale_exp(sw);
-          emax = max(emax, label);
-        }
-        int64_t total = fp4::running_term(c, p.F, emax);
-        for (int q = 0; q < ng; ++q) {
-          const int l = t * ng + q;
-          const int dq = drow[l * kDCol + scol];
-          if (dq == 0) continue;
-          const uint32_t wa = swa_row[l * mp], wb = bsw[buf][l][scol];
-          const uint32_t x = (uint32_t)(dq < 0 ? -dq : dq) * (((wa >> 16) & 0xFFu) * ((wb >> 16) & 0xFFu));
-          const int sh = p.shift0 + fp4::scale_exp(wa) + fp4::scale_exp(wb) - emax;
-          // x < 2**20 and sh <= shift0 <= 40 (a label is at least its scale exponents).
-          const int rs = max(40 - sh, 0);
-          const uint64_t v = rs >= 64 ? 0ull : (((uint64_t)x << 40) >> rs);
-          const bool neg = (dq < 0) != (((wa ^ wb) >> 24) & 1u);
-          total += neg ? -(int64_t)v : (int64_t)v;
-        }
-        c = fixed_to_fp32(total, emax, p.F, RNE, true);
+      const uint32_t swa = sas[c][lane * mp + m];
+      const int d = fp4::dot16(saq[c][lane * mp + m], bq[c]);
+      double v = 0.0;
+      int lmax = fp4::kNone, emin = fp4::kBig;
+      if (d != 0) {
+        const int e = fp4::scale_exp(swa) + eb;
+        lmax = e + (int)((swa >> 25) & 3u) + cb;
+        emin = e;
+        const int x = d * (int)(((swa >> 16) & 0xFFu) * msb);  // |x| < 2**20
+        v = (double)((((swa ^ swb[c]) >> 24) & 1u) ? -x : x) * pow2d(e - p.srad2);
       }
+      for (int o = 1; o < ng; o <<= 1) {
+        // Exact while the tile's exponent spread is at most 30 (checked by the scan before use).
+        v = __dadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+        lmax = max(lmax, __shfl_xor_sync(0xFFFFFFFFu, lmax, o));
+        emin = min(emin, __shfl_xor_sync(0xFFFFFFFFu, emin, o));
+      }
+      if (writer) p.rec[(col * p.ntiles + tile) * M + m] = TileRec{v, lmax, emin};
     }
   }
   if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicExch(p.flag, 1);
-  if (!scanner || sn >= p.N) return;
+}
+
+// The reference's exact two-pass tile step for output (m, n) (mma.py:318-336), everything recomputed
+// from global memory: exponent labels from the exponent-class masks, then the aligned, truncated
+// integer terms and the fixed-point normalisation. Taken by the rare tiles that fail the bounds.
+template <int DT, bool RNE>
+__device__ __noinline__ float exact_tile(const Fp4Args *pp, float c, int m, int64_t n, int64_t t) {
+  const Fp4Args &p = *pp;
+  const int64_t g0 = t * p.ng, g1 = min(g0 + p.ng, p.ngroups);
+  int emax = fp4::running_exp(c);
+  for (int pass = 0; pass < 2; ++pass) {
+    int64_t total = pass ? fp4::running_term(c, p.F, emax) : 0;
+    for (int64_t gi = g0; gi < g1; ++gi) {
+      Raw<DT> rr;
+      raw_load<DT>(p, n, gi, rr);
+      uint4 bq, bm;
+      uint32_t swb;
+      bool ignored = false;
+      b_group<DT>(p, n, gi, rr, bq, swb, bm, ignored);
+      const uint32_t swa = p.as[gi * p.mp + m];
+      const int d = fp4::dot16(p.aq[gi * p.mp + m], bq);
+      if (d == 0) continue;
+      if (pass == 0) {
+        const int label = fp4::exp_class_max(p.am[gi * p.mp + m], bm) + fp4::scale_exp(swa) + fp4::scale_exp(swb);
+        emax = max(emax, label);
+      } else {
+        const uint32_t x = (uint32_t)(d < 0 ? -d : d) * (((swa >> 16) & 0xFFu) * ((swb >> 16) & 0xFFu));
+        const int sh = p.shift0 + fp4::scale_exp(swa) + fp4::scale_exp(swb) - emax;
+        // x < 2**20 and sh <= shift0 <= 40 (a label is at least its scale exponents).
+        const int rs = max(40 - sh, 0);
+        const uint64_t v = rs >= 64 ? 0ull : (((uint64_t)x << 40) >> rs);
+        const bool neg = (d < 0) != (((swa ^ swb) >> 24) & 1u);
+        total += neg ? -(int64_t)v : (int64_t)v;
+      }
+    }
+    if (pass) return fixed_to_fp32(total, emax, p.F, RNE, true);
+  }
+  return c;
+}
+
+// Phase 2. One thread per output (m fastest): the K tiles in order, eight records in flight.
+template <int DT, bool RNE>
+__global__ void __launch_bounds__(128) gdfs_fp4_scan_kernel(const __grid_constant__ Fp4Args p) {
+  const int M = (int)p.M;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= p.ns * M) return;
+  const int m = (int)(idx % M);
+  const int64_t col = idx / M, n = p.n_base + col;
+  if (n >= p.N) return;
+  if (*p.flag) {  // an operand the fast path cannot take: this output by the exact generic routine
+    if (idx == 0) atomicAdd(&g_gemv_fallbacks, 1ull);
+    generic_output(p.g, m, n);
+    return;
+  }
+  const TileRec *rec = p.rec + col * p.ntiles * M + m;
+  float c = 0.0f;
+  constexpr int kBatch = 8;
+  TileRec nxt[kBatch];
+#pragma unroll
+  for (int i = 0; i < kBatch; ++i)
+    if (i < p.ntiles) nxt[i] = rec[(int64_t)i * M];
+  for (int64_t t0 = 0; t0 < p.ntiles; t0 += kBatch) {
+    TileRec cur[kBatch];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) cur[i] = nxt[i];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i)
+      if (t0 + kBatch + i < p.ntiles) nxt[i] = rec[(t0 + kBatch + i) * M];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int64_t t = t0 + i;
+      if (t >= p.ntiles) break;
+      const uint32_t cb = f2u(c) & 0x7FFFFFFFu;
+      if (cb >= kInf) break;                         // an Inf / NaN running value is sticky
+      const TileRec r = cur[i];
+      if (r.lmax == fp4::kNone) continue;            // every group sum is zero: c stays
+      const int be = (int)(cb >> 23);
+      const int lo = max(r.lmax - (p.F - 23) + 127, 1);
+      const int hi = r.emin + p.F - p.srad2 + 127;
+      const bool safe = r.lmax - r.emin <= 30 && r.lmax <= r.emin - p.srad2 + p.F &&
+                        (cb == 0 || (be >= lo && be <= hi));
+      if (safe) {
+        // Exact: both are multiples of 2**(emax'' - F) and |v| < 2**(emax'' + 4).
+        const double v = __dadd_rn(r.sum, (double)c);
+        const float rr = (RNE && fabs(v) >= 0x1p-126) ? __double2float_rn(v) : __double2float_rz(v);
+        c = fabs(v) >= 0x1p128 ? __int_as_float((int)((f2u(rr) & 0x80000000u) | kInf)) : rr;
+      } else {
+        c = exact_tile<DT, RNE>(&p, c, m, n, t);
+      }
+    }
+  }
   // Epilogue: alpha, bias, output rounding (src/tricast/reference/mma.py:376-384).
   float acc = c;
   if (p.alpha_a || p.alpha_b) {
@@ -334,61 +368,79 @@ __global__ void __launch_bounds__(kThreads) gdfs_fp4_gemv_kernel(Fp4Args p) {
     if (p.alpha_b) alpha = p.alpha_a ? __fmul_rn(alpha, *p.alpha_b) : *p.alpha_b;
     acc = __fmul_rn(alpha, acc);
   }
-  if (p.bias) acc = __fadd_rn(acc, p.bias[sn]);
+  if (p.bias) acc = __fadd_rn(acc, p.bias[n]);
   if (!p.out_plain) acc = cast_to(acc, p.of, TC_RNE, false, 0u, 32);
-  store_container(p.out, p.out_dt, (int64_t)sm * p.N + sn, acc);
+  store_container(p.out, p.out_dt, (int64_t)m * p.N + n, acc);
 }
 
 }  // namespace gemv
 
 // ---------------------------------------------------------------- host side
 struct Fp4GemvPlan {
-  int64_t ngroups, ngroups_pad;
+  int64_t ngroups, ngroups_pad, ntiles, slab;
   int mp;
-  size_t off_q, off_m, off_s, off_flag, total;
+  size_t off_q, off_m, off_s, off_rec, off_flag, total;
 };
 
-static Fp4GemvPlan plan_fp4_gemv(const GemmDesc &g) {
+// Records of at most this many bytes per slab of columns (phase 1 and 2 run once per slab).
+constexpr size_t kRecordBytes = (size_t)64 << 20;
+
+static Fp4GemvPlan plan_fp4_gemv(const GemmDesc &g, int ng) {
   Fp4GemvPlan p;
   p.ngroups = (g.K + fp4::kGS - 1) / fp4::kGS;
   p.ngroups_pad = (p.ngroups + gemv::kGroups - 1) / gemv::kGroups * gemv::kGroups;
+  p.ntiles = (p.ngroups + ng - 1) / ng;
   p.mp = 1;
   while (p.mp < g.M) p.mp *= 2;
+  const size_t per_col = (size_t)std::max<int64_t>(p.ntiles, 1) * g.M * sizeof(gemv::TileRec);
+  p.slab = std::max<int64_t>(8, (int64_t)(kRecordBytes / per_col) / 8 * 8);
+  p.slab = std::min<int64_t>(p.slab, (int64_t)65535 * 8);
+  p.slab = std::min<int64_t>(p.slab, (g.N + 7) / 8 * 8);
   const size_t recs = (size_t)p.ngroups_pad * p.mp;
   auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
   p.off_q = 0;
   p.off_m = up(recs * 16);
   p.off_s = p.off_m + up(recs * 16);
-  p.off_flag = p.off_s + up(recs * 4);
+  p.off_rec = p.off_s + up(recs * 4);
+  p.off_flag = p.off_rec + up((size_t)p.slab * per_col);
   p.total = p.off_flag + 256;
   return p;
 }
 
-size_t fp4_gemv_workspace(const GemmDesc &g) { return plan_fp4_gemv(g).total; }
+size_t fp4_gemv_workspace(const GemmDesc &g, int ng) { return plan_fp4_gemv(g, ng).total; }
+
+uint64_t gemv_exact_fallbacks() {
+  unsigned long long v = 0;
+  return cudaMemcpyFromSymbol(&v, gemv::g_gemv_fallbacks, sizeof(v)) == cudaSuccess ? (uint64_t)v : 0;
+}
 
 template <int DT, bool RNE>
-static int launch_fp4_gemv_kernel(const gemv::Fp4Args &a, cudaStream_t s) {
-  const size_t smem = 2 * (size_t)a.M * gemv::kDRow * sizeof(int32_t) + 3 * (size_t)gemv::kGroups * a.mp * 20;
-  cudaError_t e = cudaFuncSetAttribute(gemv::gdfs_fp4_gemv_kernel<DT, RNE>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return set_error(std::string("gdfs fp4 gemv: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
-  const unsigned grid = (unsigned)((a.N + gemv::kCols - 1) / gemv::kCols);
-  gemv::gdfs_fp4_gemv_kernel<DT, RNE><<<grid, gemv::kThreads, smem, s>>>(a);
-  count_launch();
+static int launch_fp4_gemv_slabs(gemv::Fp4Args a, int64_t nchunks, int64_t slab, cudaStream_t s) {
+  for (int64_t n0 = 0; n0 < a.N; n0 += slab) {
+    a.n_base = n0;
+    a.ns = std::min<int64_t>(slab, a.N - n0);
+    if (nchunks > 0) {
+      dim3 grid((unsigned)((nchunks + gemv::kChunksPerCta - 1) / gemv::kChunksPerCta), (unsigned)((a.ns + 7) / 8));
+      gemv::gdfs_fp4_tiles_kernel<DT><<<grid, gemv::kThreads, 0, s>>>(a);
+      count_launch();
+    }
+    const int64_t threads = a.ns * a.M;
+    gemv::gdfs_fp4_scan_kernel<DT, RNE><<<(unsigned)((threads + 127) / 128), 128, 0, s>>>(a);
+    count_launch();
+  }
   return TC_OK;
 }
 
 template <int DT>
-static int launch_fp4_gemv_dt(const gemv::Fp4Args &a, bool rne, cudaStream_t s) {
-  return rne ? launch_fp4_gemv_kernel<DT, true>(a, s) : launch_fp4_gemv_kernel<DT, false>(a, s);
+static int launch_fp4_gemv_dt(const gemv::Fp4Args &a, bool rne, int64_t nchunks, int64_t slab, cudaStream_t s) {
+  return rne ? launch_fp4_gemv_slabs<DT, true>(a, nchunks, slab, s) : launch_fp4_gemv_slabs<DT, false>(a, nchunks, slab, s);
 }
 
 // GDFS-FP4 for M <= 16 (the caller checked the tiled kernel's preconditions: E2M1 operands, G >= 6,
 // group size 16, K scales per multiple of 16, 23 <= F <= 48).
 int launch_fp4_gemv(const GemmDesc &g, int ng, void *workspace, size_t workspace_bytes, cudaStream_t s) {
-  const Fp4GemvPlan p = plan_fp4_gemv(g);
+  const Fp4GemvPlan p = plan_fp4_gemv(g, ng);
   if (!workspace || workspace_bytes < p.total) return set_error("tc_gemm: workspace too small"), TC_WORKSPACE_TOO_SMALL;
-  if (g.N > ((int64_t)1 << 36)) return TC_UNSUPPORTED;
   char *ws = static_cast<char *>(workspace);
   int32_t *flag = reinterpret_cast<int32_t *>(ws + p.off_flag);
   cudaMemsetAsync(flag, 0, 2 * sizeof(int32_t), s);  // [0] operands rejected, [1] timeout: both gate the generic kernel
@@ -424,6 +476,7 @@ int launch_fp4_gemv(const GemmDesc &g, int ng, void *workspace, size_t workspace
   a.aq = reinterpret_cast<const uint4 *>(ws + p.off_q);
   a.am = reinterpret_cast<const uint4 *>(ws + p.off_m);
   a.as = reinterpret_cast<const uint32_t *>(ws + p.off_s);
+  a.mp = p.mp;
   a.bv = g.b.v;
   a.bscale = g.b.skind == SK_K ? g.b.scale : nullptr;
   a.b_nkd = g.b.nkd;
@@ -436,8 +489,8 @@ int launch_fp4_gemv(const GemmDesc &g, int ng, void *workspace, size_t workspace
   a.N = g.N;
   a.K = g.K;
   a.ngroups = p.ngroups;
-  a.mp = p.mp;
   a.ng = ng;
+  a.ntiles = p.ntiles;
   const int srad = (g.a.skind == SK_K ? g.a.srad : 0) + (g.b.skind == SK_K ? g.b.srad : 0);
   a.F = g.F;
   a.shift0 = g.F - 2 - srad;
@@ -449,15 +502,18 @@ int launch_fp4_gemv(const GemmDesc &g, int ng, void *workspace, size_t workspace
   a.out_plain = g.out_is_plain;
   a.out_dt = g.out_dt;
   a.out = g.out;
+  a.rec = reinterpret_cast<gemv::TileRec *>(ws + p.off_rec);
+  a.g = g;
+  a.ngroups_pad = p.ngroups_pad;
   a.flag = flag;
+  const int64_t nchunks = p.ngroups_pad / gemv::kGroups;
   int st;
   switch (g.b.dt) {
-    case TC_F32: st = launch_fp4_gemv_dt<TC_F32>(a, g.rne, s); break;
-    case TC_BF16: st = launch_fp4_gemv_dt<TC_BF16>(a, g.rne, s); break;
-    default: st = launch_fp4_gemv_dt<TC_F16>(a, g.rne, s); break;
+    case TC_F32: st = launch_fp4_gemv_dt<TC_F32>(a, g.rne, nchunks, p.slab, s); break;
+    case TC_BF16: st = launch_fp4_gemv_dt<TC_BF16>(a, g.rne, nchunks, p.slab, s); break;
+    default: st = launch_fp4_gemv_dt<TC_F16>(a, g.rne, nchunks, p.slab, s); break;
   }
   if (st) return st;
-  launch_generic(g, flag, s);  // runs only when an operand raised the flag
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(std::string("tc_gemm gemv: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
   return TC_OK;
