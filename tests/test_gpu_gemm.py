@@ -300,3 +300,26 @@ def test_cofda_tiny_folded_scales(rows):
         assert (exact_fallbacks() == before) == fast, (exp_a, exp_b)
         want = _oracle_gemm(ta, tb, spec)
         assert bits_equal(got, want), f"{exp_a} {exp_b}: {first_mismatch(got, want)}"
+
+
+@pytest.mark.parametrize("rows", [40, 3])  # tiled kernel and small-M kernel
+@pytest.mark.parametrize("f_bits,f2_bits,chunk", [(13, 23, 32), (13, 13, 16), (21, 35, 8), (25, 48, 32), (9, 5, 32)])
+def test_cofda_decoupled_fast_path(rows, f_bits, f2_bits, chunk):
+    """Decoupled CoFDA: each chunk normalised at F from zero, then merged into the running value at
+    F2, on the fast kernels (fp32 or fp64 chunk sums, fp64 merge)."""
+    a = _quantized("fp8_tensor", rows, 1000, 61, outliers=5)
+    b = _quantized("fp8_tensor", 37, 1000, 62, scale=0.02)
+    for spec in (MMASpec("cofda", f_bits=f_bits, chunk_size=chunk, c_mode="decoupled", f2_bits=f2_bits,
+                         out_format="fp32"),
+                 MMASpec("cofda", f_bits=f_bits, chunk_size=chunk, c_mode="decoupled", f2_bits=f2_bits,
+                         out_format="bf16", norm_rounding="rne")):
+        before = exact_fallbacks()
+        got = gemm_triton(a, b, spec).float().cpu().numpy()
+        assert exact_fallbacks() == before, f"{spec}: the fast kernel declined the operands"
+        want = _oracle_gemm(a, b, spec)
+        assert bits_equal(got, want), f"{spec}: {first_mismatch(got, want)}"
+    mx_a = _quantized("mxfp8_e4m3", rows, 512, 63)
+    mx_b = _quantized("mxfp8_e4m3", 29, 512, 64, scale=0.02)
+    spec = MMASpec("cofda", f_bits=f_bits, chunk_size=chunk, c_mode="decoupled", f2_bits=f2_bits, out_format="fp32")
+    got = gemm_triton(mx_a, mx_b, spec).cpu().numpy()
+    assert bits_equal(got, _oracle_gemm(mx_a, mx_b, spec))

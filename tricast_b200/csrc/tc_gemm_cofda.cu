@@ -121,6 +121,7 @@ struct Args {
   const float *sa, *sb;          // promote K scales (or nullptr)
   int64_t sa_nkd, sb_nkd;
   int sa_kd, sb_kd, CS;
+  int dec, F2;                   // decoupled accumulator (no promotion) and its merge radix
   GemmDesc g;                    // epilogue (scales, alpha, bias, output)
   const int32_t *flag;
   int32_t *status;
@@ -188,7 +189,8 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
     for (int q = 0; q < 2; ++q)
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        em2[q][j] = ((uint32_t)running_exp(c[2 * q][j]) & 0xFFFFu) | ((uint32_t)running_exp(c[2 * q + 1][j]) << 16);
+        em2[q][j] = p.dec ? (((uint32_t)kZeroExp & 0xFFFFu) | ((uint32_t)kZeroExp << 16))  // decoupled: c not in the chunk
+                          : ((uint32_t)running_exp(c[2 * q][j]) & 0xFFFFu) | ((uint32_t)running_exp(c[2 * q + 1][j]) << 16);
 #pragma unroll 8
     for (int kk = 0; kk < CS; ++kk) {
       const uint2 ea = *reinterpret_cast<const uint2 *>(&st.ae[kk][ty * 2]);
@@ -209,7 +211,7 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
         const uint32_t w = em2[i >> 1][j];
         emax[i][j] = (int)(int16_t)((i & 1) ? (w >> 16) : (w & 0xFFFFu));
         S[i][j] = Acc<T>::pow2(F - emax[i][j]);
-        tot[i][j] = Acc<T>::running(c[i][j], F, emax[i][j], S[i][j]);
+        tot[i][j] = p.dec ? (T)0 : Acc<T>::running(c[i][j], F, emax[i][j], S[i][j]);
       }
     // Pass 2: exact aligned sum.
 #pragma unroll 4
@@ -228,8 +230,12 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
-        if (cb >= kInf) continue;  // an overflowed running value is sticky (operands are finite)
-        c[i][j] = Acc<T>::finish(tot[i][j], emax[i][j], F, RNE);
+        const float r = Acc<T>::finish(tot[i][j], emax[i][j], F, RNE);
+        if (p.dec) {
+          c[i][j] = merge_decoupled(r, c[i][j], p.F2, RNE);
+        } else if (cb < kInf) {  // an overflowed running value is sticky (operands are finite)
+          c[i][j] = r;
+        }
       }
     if (p.PI_chunks && (ch + 1) % p.PI_chunks == 0 || p.PI_chunks && ch + 1 == p.nchunks) {
       // End of a promote interval: acc = fma(partial, (1 * sa) * sb, acc), partial restarts at 0.
@@ -274,7 +280,8 @@ static bool narrow_float(const Fmt &f) { return f.kind == 0 && f.mbits <= 3 && f
 static CofdaPlan plan_cofda(const GemmDesc &g) {
   CofdaPlan p;
   std::memset(&p, 0, sizeof(p));
-  if (g.alg != ALG_COFDA || g.decoupled) return p;
+  if (g.alg != ALG_COFDA) return p;
+  if (g.decoupled && !g.PI && (g.F2 < 1 || g.F2 > 50)) return p;  // the fp64 merge needs F2 <= 50
   if (g.CS != 8 && g.CS != 16 && g.CS != 32) return p;
   if (!narrow_float(g.a.f) || !narrow_float(g.b.f)) return p;
   int width_bits = 0;
@@ -388,6 +395,8 @@ int launch_cofda(const GemmDesc &g, void *workspace, size_t workspace_bytes, cud
     if (g.a.skind == SK_K) { a.sa = g.a.scale; a.sa_nkd = g.a.nkd; a.sa_kd = g.a.kd; }
     if (g.b.skind == SK_K) { a.sb = g.b.scale; a.sb_nkd = g.b.nkd; a.sb_kd = g.b.kd; }
   }
+  a.dec = g.decoupled && !g.PI;  // with a promote interval the reference accumulates fused
+  a.F2 = g.F2;
   a.g = g;
   a.flag = flag;
   a.status = flag + 1;

@@ -47,6 +47,7 @@ struct Args {
   Fmt bsf;
   int64_t M, N, K, nchunks;
   int F, cols, KC, rne, PI_chunks;
+  int dec, F2;               // decoupled accumulator (no promotion) and its merge radix
   const float *sa, *sb;      // promote K scales or nullptr
   int64_t sa_nkd, sb_nkd;
   int sa_kd, sb_kd;
@@ -329,15 +330,16 @@ __global__ void __launch_bounds__(kThreads) cofda_gemv_kernel(Args<T> p) {
 #pragma unroll
       for (int i = 0; i < PL; ++i) pe = max(pe, ea[i] + eb[i]);
       pe = group_max<LG>(pe);
-      const int emax = max(cofda::running_exp(c), pe);
+      const int emax = p.dec ? pe : max(cofda::running_exp(c), pe);  // decoupled: c is not in the chunk
       const T S = cofda::Acc<T>::pow2(p.F - emax);
       T tot = (T)0;
 #pragma unroll
       for (int i = 0; i < PL; ++i) tot = cofda::Acc<T>::add(tot, cofda::Acc<T>::trunc(cofda::Acc<T>::mul(a[i], b[i]), S));
       tot = group_sum<LG, T>(tot);
-      tot = cofda::Acc<T>::add(tot, cofda::Acc<T>::running(c, p.F, emax, S));
+      if (!p.dec) tot = cofda::Acc<T>::add(tot, cofda::Acc<T>::running(c, p.F, emax, S));
       const float nc = cofda::Acc<T>::finish(tot, emax, p.F, p.rne != 0);
-      c = (f2u(c) & 0x7FFFFFFFu) >= kInf ? c : nc;  // an overflowed running value is sticky
+      if (p.dec) c = cofda::merge_decoupled(nc, c, p.F2, p.rne != 0);
+      else c = (f2u(c) & 0x7FFFFFFFu) >= kInf ? c : nc;  // an overflowed running value is sticky
       if (p.PI_chunks && ((gch + 1) % p.PI_chunks == 0 || gch + 1 == p.nchunks)) {
         // End of a promote interval: acc = fma(partial, (1 * sa) * sb, acc), partial restarts at 0.
         const int64_t begin = (gch / p.PI_chunks) * (int64_t)p.PI_chunks * CS;
@@ -453,6 +455,8 @@ static int launch_cofda_gemv_typed(const GemmDesc &g, const CofdaGemvPlan &p, ch
   a.F = g.F;
   a.rne = g.rne;
   a.PI_chunks = g.apply == AP_PROMOTE ? g.PI / g.CS : 0;
+  a.dec = g.decoupled && !g.PI;  // with a promote interval the reference accumulates fused
+  a.F2 = g.F2;
   if (g.apply == AP_PROMOTE) {
     if (g.a.skind == SK_K) { a.sa = g.a.scale; a.sa_nkd = g.a.nkd; a.sa_kd = g.a.kd; }
     if (g.b.skind == SK_K) { a.sb = g.b.scale; a.sb_nkd = g.b.nkd; a.sb_kd = g.b.kd; }
