@@ -68,6 +68,25 @@ def test_resolve_scale_apply():
         resolve_scale_apply(PRESETS["int_exact"], _op("k", kd=32), _op("none"))
 
 
+def test_scale_domain_crossing_matches_full_scan():
+    """resolve_scale_apply decides domain crossings from one period of lcm(span, k_domain); the
+    decision equals the reference's scan over every interval."""
+    def full(K, span, kd):
+        return any(s // kd != (min(s + span, K) - 1) // kd for s in range(0, K, span))
+
+    for K in (1, 7, 16, 64, 100, 1000, 4096):
+        for span in (1, 3, 16, 24, 32, 128):
+            for kd in (1, 5, 16, 32, 48, 128):
+                op = SimpleNamespace(scale_kind="k", K=K, k_domain=kd)
+                spec = MMASpec("cofda", f_bits=13, chunk_size=1, promote_interval=span)
+                try:
+                    resolve_scale_apply(spec, op, SimpleNamespace(scale_kind="none"))
+                    raised = False
+                except ValueError:
+                    raised = True
+                assert raised == full(K, span, kd), (K, span, kd)
+
+
 def test_headroom():
     int8 = F.INT8
     a = _op("none", fmt=int8)

@@ -10,6 +10,7 @@ copy is made.
 from __future__ import annotations
 
 import ctypes as C
+import math
 
 import torch
 
@@ -39,8 +40,11 @@ def resolve_scale_apply(spec, a, b) -> str:
         raise ValueError(f"{spec.algorithm}: K-varying scales cannot be applied in the epilogue")
     span = spec.group_size if mode == "group" else spec.promote_interval if mode == "promote" else 0
     for op in k_scaled:
+        # An interval starting at s crosses a domain boundary iff the one starting at s + lcm(span,
+        # k_domain) does (same offset inside its domain, never longer), so the first period decides.
+        stop = min(op.K, span * op.k_domain // math.gcd(span, op.k_domain)) if span else 0
         if span and any(start // op.k_domain != (min(start + span, op.K) - 1) // op.k_domain
-                        for start in range(0, op.K, span)):
+                        for start in range(0, stop, span)):
             raise ValueError(f"{mode} interval/group size {span} crosses K scale domain {op.k_domain}")
     return mode
 
