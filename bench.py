@@ -156,6 +156,56 @@ def measure_gemm_config(dev, name: str, steps: int, warmup: int) -> dict:
     return {"workload": name, "shape": [m, n, k], "gmacs": m * n * k / (t * 1e-3) / 1e9, "ms": t}
 
 
+def measure_decode(dev, calls: int = 200) -> list:
+    """Decode-shaped steps (one token: A is 1 x 4096, B a pre-quantized 4096 x 4096 weight): quantize
+    the activation + emulated GEMM, through the public API. ``call_us``: wall time per step over
+    back-to-back calls (host work included, one synchronisation at the end); ``gpu_us``: device time
+    of one step replayed from a CUDA graph, L2 flushed before each replay."""
+    import torch
+
+    from tricast_b200 import as_operand, gemm_triton, quantize_triton
+    from tricast_b200.spec import PRESETS, SCHEMES
+
+    g = torch.Generator().manual_seed(7)
+    w = (torch.randn(4096, 4096, generator=g) * 0.02).bfloat16().to(dev)
+    x = torch.randn(1, 4096, generator=g).bfloat16().to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    out = []
+    for scheme, preset in (("nvfp4", "nvidia_blackwell_fp4"), ("fp8_tensor", "nvidia_hopper_fp8")):
+        b = as_operand(quantize_triton(w, SCHEMES[scheme]), compact=True)
+        spec = PRESETS[preset].with_(out_format="fp32")
+
+        def step():
+            return gemm_triton(as_operand(quantize_triton(x, SCHEMES[scheme]), compact=True), b, spec)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for _ in range(calls):
+            step()
+        torch.cuda.synchronize(dev)
+        call_us = (time.perf_counter() - t0) / calls * 1e6
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        times = []
+        for _ in range(20):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1) * 1e3)
+        del graph
+        times.sort()
+        out.append({"workload": f"decode M=1 {scheme} x {preset} 1x4096x4096 (quantize activation + GEMM)",
+                    "call_us": call_us, "gpu_us": times[len(times) // 2]})
+    return out
+
+
 def make_inputs(rank: int):
     """Seeded CPU generation so every GPU count sees identical tensors."""
     import torch
@@ -436,6 +486,7 @@ def run_b200(args) -> None:
         if world == 1:
             line["aux_cast"] = measure_cfg1(dev, args.steps, args.warmup)
             line["aux_gemm"] = [measure_gemm_config(dev, c, max(2, args.steps // 3), 1) for c in ("cfg3", "cfg4")]
+            line["aux_decode"] = measure_decode(dev)
         if world == 1 and not args.no_cpu_baseline:
             v, desc = cpu_oracle_sample(32, 512)
             line["cpu_baseline"] = {"value": v, "unit": "GMAC/s", "cores": 1, "kind": "port", "sample": desc}
