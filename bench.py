@@ -503,8 +503,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1", "cfg3", "cfg4"],
-                    help="cfg1/cfg3/cfg4 run only that measurement (for profiling)")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1", "cfg3", "cfg4", "decode"],
+                    help="cfg1/cfg3/cfg4/decode run only that measurement (for profiling)")
     args = ap.parse_args()
     if args.workload != "cfg2" and args.impl != "reference":
         import torch
@@ -512,6 +512,8 @@ def main() -> None:
         dev = torch.device("cuda", 0)
         if args.workload == "cfg1":
             print(json.dumps(measure_cfg1(dev, args.steps, args.warmup)))
+        elif args.workload == "decode":
+            print(json.dumps(measure_decode(dev, calls=args.steps)))
         else:
             print(json.dumps(measure_gemm_config(dev, args.workload, args.steps, args.warmup)))
         return
