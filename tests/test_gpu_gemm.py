@@ -323,3 +323,33 @@ def test_cofda_decoupled_fast_path(rows, f_bits, f2_bits, chunk):
     spec = MMASpec("cofda", f_bits=f_bits, chunk_size=chunk, c_mode="decoupled", f2_bits=f2_bits, out_format="fp32")
     got = gemm_triton(mx_a, mx_b, spec).cpu().numpy()
     assert bits_equal(got, _oracle_gemm(mx_a, mx_b, spec))
+
+
+@pytest.mark.parametrize("shape", [(130, 260, 384), (1, 1, 128), (128, 128, 128), (257, 129, 1000)])
+def test_int_tensor_core_path(shape):
+    """Integer operands on the tcgen05 kind::i8 kernel: promoted CoFDA intervals (INT8 row-scaled x
+    INT5 with FP16 K scales per 128) and int_exact, ragged tiles and spans, bit-exact and without the
+    exact fallback."""
+    m, n, k = shape
+    g = torch.Generator().manual_seed(sum(shape))
+    x = torch.randn(m, k, generator=g)
+    w = torch.randn(n, k, generator=g) * 0.02
+    qa = quantize_triton(x.cuda(), SCHEMES["int8_row"])
+    qw = quantize_triton(w.cuda(), SCHEMES["int4_g128_zp"])
+    z = qw.zero_point.repeat_interleave(128, dim=1)[:, :k]
+    a = as_operand(qa)
+    b = Operand(qw.values.float() - z, IntFormat("int5", 5), qw.scale, FP16, "k", 128)
+    spec = MMASpec("cofda", f_bits=23, chunk_size=32, promote_interval=128, out_format="fp32")
+    before = exact_fallbacks()
+    got = gemm_triton(a, b, spec).cpu().numpy()
+    assert exact_fallbacks() == before, "the tensor-core kernel declined or timed out"
+    want = _oracle_gemm(a, b, spec)
+    assert bits_equal(got, want), first_mismatch(got, want)
+    ia = Operand(qa.values.float(), IntFormat("int8", 8))
+    ib = Operand(qw.values.float() - z, IntFormat("int5", 5))
+    spec = MMASpec("int_exact", out_format="fp32")
+    before = exact_fallbacks()
+    got = gemm_triton(ia, ib, spec).cpu().numpy()
+    assert exact_fallbacks() == before, "the tensor-core kernel declined or timed out"
+    want = _oracle_gemm(ia, ib, spec)
+    assert bits_equal(got, want), first_mismatch(got, want)

@@ -38,6 +38,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   return false;
 }
 
+// Bounded wait that lets the hardware suspend the thread between polls (up to ~64 us each), so
+// waiting warps do not take issue slots from working ones; gives up after ~2**16 polls (seconds).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity) {
+  for (int i = 0; i < (1 << 16); ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(0x10000u)
+        : "memory");
+    if (ok) return true;
+    __nanosleep(32);
+  }
+  return false;
+}
+
 // Global -> this CTA's shared memory, completing `bytes` on `bar`. Both addresses 16-byte aligned,
 // bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

@@ -240,14 +240,16 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
     if (p.PI_chunks && (ch + 1) % p.PI_chunks == 0 || p.PI_chunks && ch + 1 == p.nchunks) {
       // End of a promote interval: acc = fma(partial, (1 * sa) * sb, acc), partial restarts at 0.
       const int64_t begin = (ch / p.PI_chunks) * (int64_t)p.PI_chunks * CS;
+      const float *sac = p.sa ? p.sa + begin / p.sa_kd : nullptr;  // one division per interval
+      const float *sbc = p.sb ? p.sb + begin / p.sb_kd : nullptr;
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int64_t m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
           float w = 1.0f;
-          if (p.sa && m < p.M) w = __fmul_rn(w, p.sa[m * p.sa_nkd + begin / p.sa_kd]);
-          if (p.sb && n < p.N) w = __fmul_rn(w, p.sb[n * p.sb_nkd + begin / p.sb_kd]);
+          if (sac && m < p.M) w = __fmul_rn(w, sac[m * p.sa_nkd]);
+          if (sbc && n < p.N) w = __fmul_rn(w, sbc[n * p.sb_nkd]);
           acc[i][j] = __fmaf_rn(c[i][j], w, acc[i][j]);
           c[i][j] = 0.0f;
         }

@@ -176,17 +176,20 @@ __global__ void __launch_bounds__(256) int_kernel(Args p) {
         for (int j = 0; j < 8; ++j) d[i][j] = __dp4a(av[i], bv[j], d[i][j]);
     }
     if (PROMOTE) {
+      // This interval's scale columns (one division per span, not per output).
       const int64_t begin = sp * kSpan;
+      const float *sac = p.sa ? p.sa + begin / p.sa_kd : nullptr;
+      const float *sbc = p.sb ? p.sb + begin / p.sb_kd : nullptr;
       float wa[8], wb[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int64_t m = mt * kTile + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
-        wa[i] = (p.sa && m < p.M) ? p.sa[m * p.sa_nkd + begin / p.sa_kd] : 1.0f;
+        wa[i] = (sac && m < p.M) ? sac[m * p.sa_nkd] : 1.0f;
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int64_t n = nt * kTile + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
-        wb[j] = (p.sb && n < p.N) ? p.sb[n * p.sb_nkd + begin / p.sb_kd] : 1.0f;
+        wb[j] = (sbc && n < p.N) ? sbc[n * p.sb_nkd] : 1.0f;
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i)
@@ -259,14 +262,28 @@ static IntPlan plan_int(const GemmDesc &g) {
   return p;
 }
 
+// Tensor-core version (tc_gemm_int_tc.cu): the same exact integers from tcgen05.mma kind::i8.
+bool int_tc_eligible(const GemmDesc &g, bool promote, int64_t max_a, int64_t max_b);
+size_t int_tc_workspace(const GemmDesc &g);
+int launch_int_tc(const GemmDesc &g, bool promote, void *workspace, size_t workspace_bytes, cudaStream_t s);
+
+static bool use_tc(const GemmDesc &g, const IntPlan &p) {
+  return p.nspans > 0 && int_tc_eligible(g, p.promote, int_max_abs(g.a.f), int_max_abs(g.b.f));
+}
+
 size_t int_workspace(const GemmDesc &g) {
   IntPlan p = plan_int(g);
-  return p.ok ? p.total : 0;
+  if (!p.ok) return 0;
+  return use_tc(g, p) ? int_tc_workspace(g) : p.total;
 }
 
 int launch_int(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s) {
   IntPlan p = plan_int(g);
   if (!p.ok) return TC_UNSUPPORTED;
+  if (use_tc(g, p)) {
+    const int st = launch_int_tc(g, p.promote, workspace, workspace_bytes, s);
+    if (st != TC_UNSUPPORTED) return st;
+  }
   if (!workspace || workspace_bytes < p.total) return set_error("tc_gemm: workspace too small"), TC_WORKSPACE_TOO_SMALL;
   if ((g.M + intk::kTile - 1) / intk::kTile > 65535) return TC_UNSUPPORTED;
   char *ws = static_cast<char *>(workspace);
