@@ -36,7 +36,7 @@ WORKLOAD = ("cfg2 NVFP4 W4A4 emulated GEMM 2048x4096x4096: quantize A,B (nvfp4) 
 L2_FLUSH_BYTES = 512 << 20
 # dram__bytes_read.sum + dram__bytes_write.sum of one gdfs_fp4_kernel<4> launch on cfg2 (one ncu
 # --set full capture of this bench's first timed step).
-GDFS_TRAFFIC_BYTES = 45_354_752 + 9_424_896
+GDFS_TRAFFIC_BYTES = 40_644_352 + 3_510_272
 
 
 CFG1_BYTES_PER_ELEM = 4 + 4 + 0.5 + 1 / 32  # fp32 in, fp32 dequant out, E2M1 nibble, E8M0 byte per 32
@@ -204,6 +204,40 @@ def measure_decode(dev, calls: int = 200) -> list:
         out.append({"workload": f"decode M=1 {scheme} x {preset} 1x4096x4096 (quantize activation + GEMM)",
                     "call_us": call_us, "gpu_us": times[len(times) // 2]})
     return out
+
+
+def measure_cfg2_step(dev, steps: int, warmup: int) -> dict:
+    """The headline step alone (quantize A and B to NVFP4 + Blackwell-FP4 GEMM, inputs resident, L2
+    flushed between steps): a short, focused run for profilers."""
+    import torch
+
+    from tricast_b200 import as_operand, gemm_triton, quantize_triton
+    from tricast_b200.spec import PRESETS, SCHEMES
+
+    a_cpu, b_cpu = make_inputs(0)
+    a, b = a_cpu.to(dev), b_cpu.to(dev)
+    spec_q, spec_m = SCHEMES["nvfp4"], PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        qa, qb = quantize_triton(a, spec_q), quantize_triton(b, spec_q)
+        return gemm_triton(as_operand(qa, compact=True), as_operand(qb, compact=True), spec_m)
+
+    for _ in range(warmup):
+        step()
+    times = []
+    for _ in range(steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step()
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    t = sum(times) / len(times)
+    m, n, k = a.shape[0], b.shape[0], a.shape[1]
+    return {"workload": "cfg2 step", "shape": [m, n, k], "gmacs": m * n * k / (t * 1e-3) / 1e9, "ms": t}
 
 
 def make_inputs(rank: int):
@@ -473,9 +507,11 @@ def run_b200(args) -> None:
             "gpu_launches": int(launches),
             "roofline": {"bound": "alu", "achieved": achieved, "peak": peak_gmacs, "unit": "GMAC/s",
                          "frac": achieved / peak_gmacs, "traffic": GDFS_TRAFFIC_BYTES,
-                         "note": f"emulated GEMM (encode + GDFS kernel, CUDA events); peak = 148 SMs x "
-                                 f"{dp4a_lanes} DP4A lanes x 4 MAC x {sm_mhz:.0f} MHz; traffic = DRAM bytes "
-                                 "per GDFS launch from one ncu capture"},
+                         "note": f"emulated GEMM (encode + GDFS kernel, CUDA events); the group dot products "
+                                 "run on tcgen05 int8 MMAs and the exact int64/fp64 tile arithmetic on the CUDA "
+                                 f"cores bounds the kernel; peak = the CUDA-core DP4A rate, 148 SMs x {dp4a_lanes} "
+                                 f"lanes x 4 MAC x {sm_mhz:.0f} MHz; traffic = DRAM bytes per GDFS launch from one "
+                                 "ncu capture"},
             "gemm_ms": t_gemm,
             "aux_sweep": {"workload": "cfg5 per-layer error sweep: 196 Qwen3-0.6B-shaped layers x "
                                       "(MXFP4, NVFP4, FP8 E4M3, INT4-g128) vs fp64, 2048 tokens",
@@ -503,8 +539,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1", "cfg3", "cfg4", "decode"],
-                    help="cfg1/cfg3/cfg4/decode run only that measurement (for profiling)")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg2step", "cfg1", "cfg3", "cfg4", "decode"],
+                    help="cfg2step/cfg1/cfg3/cfg4/decode run only that measurement (for profiling)")
     args = ap.parse_args()
     if args.workload != "cfg2" and args.impl != "reference":
         import torch
@@ -512,6 +548,8 @@ def main() -> None:
         dev = torch.device("cuda", 0)
         if args.workload == "cfg1":
             print(json.dumps(measure_cfg1(dev, args.steps, args.warmup)))
+        elif args.workload == "cfg2step":
+            print(json.dumps(measure_cfg2_step(dev, args.steps, args.warmup)))
         elif args.workload == "decode":
             print(json.dumps(measure_decode(dev, calls=args.steps)))
         else:

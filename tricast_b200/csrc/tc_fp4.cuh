@@ -202,5 +202,26 @@ __device__ __forceinline__ int64_t running_term(float c, int F, int emax) {
   return (f2u(c) >> 31) ? -(int64_t)v : (int64_t)v;
 }
 
+// Arguments of the GDFS-FP4 GEMM kernels (tiled DP4A and tensor-core): the encoded records of both
+// operands, the GDFS radices and the epilogue.
+struct GemmArgs {
+  const uint4 *aq, *am, *bq, *bm;
+  const uint32_t *as, *bs;        // scale words (exact path)
+  const int32_t *amul, *bmul;     // multipliers [ntiles * ng][rows_pad]
+  const int2 *atw, *btw;          // tile words [ntiles][rows_pad]
+  int64_t a_rows_pad, b_rows_pad;
+  int64_t M, N, ntiles;
+  int F, shift0;       // shift0 = F - 2 - srad (srad = radix of the combined scale)
+  int srad2;           // srad + 2: a group value is sx * 2**(es_a + es_b - srad2)
+  int pexp;            // 1023 - srad2: fp64 exponent field offset of those powers of two
+  int rne;
+  const float *alpha_a, *alpha_b, *bias;
+  Fmt of;
+  int out_plain, out_dt;
+  void *out;
+  const int32_t *flag;   // nonzero: the fast path is not valid for these operands
+  int32_t *status;       // set to 1 when a bounded wait gives up
+};
+
 }  // namespace fp4
 }  // namespace tc

@@ -161,25 +161,6 @@ __global__ void __launch_bounds__(256) tile_words_kernel(const uint32_t *__restr
   }
 }
 
-struct GemmArgs {
-  const uint4 *aq, *am, *bq, *bm;
-  const uint32_t *as, *bs;        // scale words (exact path)
-  const int32_t *amul, *bmul;     // multipliers [ntiles * ng][rows_pad]
-  const int2 *atw, *btw;          // tile words [ntiles][rows_pad]
-  int64_t a_rows_pad, b_rows_pad;
-  int64_t M, N, ntiles;
-  int F, shift0;       // shift0 = F - 2 - srad (srad = radix of the combined scale)
-  int srad2;           // srad + 2: a group value is sx * 2**(es_a + es_b - srad2)
-  int pexp;            // 1023 - srad2: fp64 exponent field offset of those powers of two
-  int rne;
-  const float *alpha_a, *alpha_b, *bias;
-  Fmt of;
-  int out_plain, out_dt;
-  void *out;
-  const int32_t *flag;   // nonzero: the fast path is not valid for these operands
-  int32_t *status;       // set to 1 when a bounded wait gives up
-};
-
 template <int NG>
 struct Stage {
   uint4 aq[NG][kTileRows];
@@ -441,7 +422,7 @@ static Fp4Plan plan_fp4(const GemmDesc &g) {
   p.ng = g.KT / fp4::kGS;
   if (p.ng != 1 && p.ng != 2 && p.ng != 4 && p.ng != 8) return p;
   p.ntiles = (g.K + g.KT - 1) / g.KT;
-  p.a_pad = (g.M + fp4::kTileRows - 1) / fp4::kTileRows * fp4::kTileRows;
+  p.a_pad = (g.M + 127) / 128 * 128;  // whole 128-row tiles for the tensor-core kernel (64 for the DP4A one)
   p.b_pad = (g.N + fp4::kTileRows - 1) / fp4::kTileRows * fp4::kTileRows;
   int64_t ga = p.ntiles * p.ng * p.a_pad, gb = p.ntiles * p.ng * p.b_pad;
   size_t sizes[10] = {(size_t)ga * 16, (size_t)ga * 16, (size_t)ga * 4, (size_t)ga * 4, (size_t)(p.ntiles * p.a_pad) * 8,
@@ -465,6 +446,7 @@ size_t int_workspace(const GemmDesc &g);
 int launch_fma(const GemmDesc &g, cudaStream_t s);
 int launch_int(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
 
+int launch_fp4_gemm_tc(const fp4::GemmArgs &args, int ng, cudaStream_t s);
 size_t fp4_gemv_workspace(const GemmDesc &g, int ng);
 int launch_fp4_gemv(const GemmDesc &g, int ng, void *workspace, size_t workspace_bytes, cudaStream_t s);
 
@@ -575,8 +557,8 @@ int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
   a.out = g.out;
   a.flag = flag;
   a.status = flag + 1;
-  int st;
-  switch (p.ng) {
+  int st = launch_fp4_gemm_tc(a, p.ng, s);  // tensor cores for NG <= 4
+  if (st == TC_UNSUPPORTED) switch (p.ng) {
     case 1: st = launch_fp4_gemm<1>(a, g.M, g.N, s); break;
     case 2: st = launch_fp4_gemm<2>(a, g.M, g.N, s); break;
     case 4: st = launch_fp4_gemm<4>(a, g.M, g.N, s); break;

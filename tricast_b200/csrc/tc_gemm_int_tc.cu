@@ -26,6 +26,7 @@
 
 #include "tc_bulk.cuh"
 #include "tc_gemm.cuh"
+#include "tc_tcgen05.cuh"
 
 namespace tc {
 namespace itc {
@@ -103,49 +104,8 @@ struct Args {
   int32_t *status;
 };
 
-// UMMA shared-memory descriptor, K-major, no swizzle (sm100 version 1): start address, leading byte
-// offset (K direction) and stride byte offset (M/N direction), all in 16-byte units.
-__device__ __forceinline__ uint64_t smem_desc(const void *p, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-  const uint64_t addr = (uint64_t)((smem_addr(p) >> 4) & 0x3FFFu);
-  return addr | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) | ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) |
-         (1ull << 46);  // version 1; base offset 0, legacy LBO mode, layout type 0 (no swizzle)
-}
-
 // Instruction descriptor: kind::i8, D int32, A and B signed int8, both K-major, M = 128, N = 128.
-constexpr uint32_t kIdesc = (2u << 4)       // D format S32
-                            | (1u << 7)     // A signed 8-bit
-                            | (1u << 10)    // B signed 8-bit
-                            | ((uint32_t)(kTile >> 3) << 17)   // N >> 3
-                            | ((uint32_t)(kTile >> 4) << 24);  // M >> 4
-
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %3, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %4, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(accumulate), "r"(kIdesc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 32 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
+constexpr uint32_t kIdesc = tc5::idesc_i8(kTile, kTile);
 
 template <bool PROMOTE>
 __global__ void __launch_bounds__(kThreads, 1) int_tc_kernel(Args p) {
@@ -166,14 +126,10 @@ __global__ void __launch_bounds__(kThreads, 1) int_tc_kernel(Args p) {
     }
     fence_barrier_init();
   }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
-                 "r"(kTmemCols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
-  }
-  fence_before_sync();
+  if (warp == 0) tc5::tmem_alloc(&tmem_base, kTmemCols);
+  tc5::fence_before_sync();
   __syncthreads();
-  fence_after_sync();
+  tc5::fence_after_sync();
   const uint32_t tbase = tmem_base;
 
   if (warp == kEpilogueWarps) {
@@ -197,16 +153,16 @@ __global__ void __launch_bounds__(kThreads, 1) int_tc_kernel(Args p) {
         if (PROMOTE && sp >= 2 && !mbar_wait_sleep(&tempty[b], (uint32_t)(((sp - 2) >> 1) & 1))) { ok = false; break; }
         if (!mbar_wait_sleep(&full[s], (uint32_t)((sp / kStages) & 1))) { ok = false; break; }
         waited_full = sp + 1;
-        fence_after_sync();
+        tc5::fence_after_sync();
         const unsigned char *sa = smem_raw + (size_t)s * 2 * kSpanBytes, *sb = sa + kSpanBytes;
 #pragma unroll
         for (int kk = 0; kk < kSpan / 32; ++kk) {
-          const uint64_t da = smem_desc(sa + kk * 2 * (kTile * 16), kTile * 16, 128);
-          const uint64_t db = smem_desc(sb + kk * 2 * (kTile * 16), kTile * 16, 128);
-          mma_i8(tbase + (uint32_t)(b * kTile), da, db, (PROMOTE ? kk > 0 : (sp > 0 || kk > 0)) ? 1u : 0u);
+          const uint64_t da = tc5::smem_desc(sa + kk * 2 * (kTile * 16), kTile * 16, 128);
+          const uint64_t db = tc5::smem_desc(sb + kk * 2 * (kTile * 16), kTile * 16, 128);
+          tc5::mma_i8(tbase + (uint32_t)(b * kTile), da, db, kIdesc, (PROMOTE ? kk > 0 : (sp > 0 || kk > 0)) ? 1u : 0u);
         }
-        mma_commit(&empty[s]);                          // the stage is free once these MMAs finish
-        if (PROMOTE || sp == p.nspans - 1) mma_commit(&tfull[b]);  // the partial is ready
+        tc5::mma_commit(&empty[s]);                          // the stage is free once these MMAs finish
+        if (PROMOTE || sp == p.nspans - 1) tc5::mma_commit(&tfull[b]);  // the partial is ready
         last = sp;
         // Refill the stage of span sp - 1 (its MMAs run ahead of the ones just queued) with the span
         // kStages after it, so the tensor pipe always has the next span's MMAs queued.
@@ -242,10 +198,10 @@ __global__ void __launch_bounds__(kThreads, 1) int_tc_kernel(Args p) {
         ok = false;
         break;
       }
-      fence_after_sync();
+      tc5::fence_after_sync();
       uint32_t d[32];
-      tmem_ld32(lane_addr + (uint32_t)(b * kTile), d);
-      fence_before_sync();
+      tc5::tmem_ld32(lane_addr + (uint32_t)(b * kTile), d);
+      tc5::fence_before_sync();
       __syncwarp();
       if (PROMOTE && lane == 0) mbar_arrive(&tempty[b]);  // the buffer may take span sp + 2
       if (PROMOTE) {
@@ -276,10 +232,10 @@ __global__ void __launch_bounds__(kThreads, 1) int_tc_kernel(Args p) {
       }
     }
   }
-  fence_before_sync();
+  tc5::fence_before_sync();
   __syncthreads();
-  fence_after_sync();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kTmemCols));
+  tc5::fence_after_sync();
+  if (warp == 0) tc5::tmem_dealloc(tbase, kTmemCols);
 }
 
 }  // namespace itc
