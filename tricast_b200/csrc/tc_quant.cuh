@@ -160,6 +160,23 @@ __device__ __forceinline__ float unkey(uint32_t k) { return u2f((k & 0x80000000u
 // Integer rounding for zero-point specs on the unbounded integer grid, then + z and clamp
 // (src/tricast/reference/quantize.py:325-332).
 __device__ __forceinline__ float zp_round(float xq, float z, const QParams &p, uint32_t noise) {
+  if (p.rnd != TC_SR && p.qmax_d < 16777216.0 && p.qmin_d > -16777216.0) {
+    // Deterministic modes in fp32 (integer grids inside +-2**24): rint / trunc / ceil / floor / round
+    // give the integer the reference forms on |xq| (its direction rules per sign are exactly these),
+    // NaN and Inf pass through; an integer zero point then adds exactly (both integers below 2**24;
+    // any larger sum lies beyond the clamp and clamps to the same bound), and the compare-and-select
+    // clamp keeps NaN as the reference's does.
+    const float k = p.rnd == TC_RNE ? rintf(xq)
+                    : p.rnd == TC_RTZ ? truncf(xq)
+                    : p.rnd == TC_RUP ? ceilf(xq)
+                    : p.rnd == TC_RDN ? floorf(xq)
+                                      : roundf(xq);
+    float r = p.zp == ZP_INT ? __fadd_rn(k, z) : k;
+    const float lo = (float)p.qmin_d, hi = (float)p.qmax_d;
+    if (r < lo) r = lo;
+    if (r > hi) r = hi;
+    return r;
+  }
   uint32_t u = f2u(xq);
   uint32_t a = u & 0x7FFFFFFFu;
   double r;
