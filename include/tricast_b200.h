@@ -192,6 +192,14 @@ uint64_t tc_launch_count(void);
  * device. */
 int tc_exact_fallbacks(uint64_t *count);
 
+/* Silicon probe, not part of the emulation API: out[M][N] = sum_k A[m][k] * B[n][k] computed by the
+ * B200's own FP8 tensor-core MMA (tcgen05.mma kind::f8f6f4, fp32 accumulator, K issued 32 at a time
+ * in order, no scales). a [M][K] and b [N][K] are row-major 8-bit codes, fmt 0 = E4M3, 1 = E5M2;
+ * out is fp32 [M][N]. *status (device) is set non-zero if a wait inside the kernel ran out. Used to
+ * test whether an emulated accumulation model reproduces the hardware; no reference interface. */
+int tc_probe_mma_fp8(const uint8_t *a, const uint8_t *b, int64_t M, int64_t N, int64_t K, int32_t fmt, float *out,
+                     int32_t *status, tc_stream stream);
+
 /* Library version string. */
 const char *tc_version(void);
 
