@@ -200,6 +200,14 @@ int tc_exact_fallbacks(uint64_t *count);
 int tc_probe_mma_fp8(const uint8_t *a, const uint8_t *b, int64_t M, int64_t N, int64_t K, int32_t fmt, float *out,
                      int32_t *status, tc_stream stream);
 
+/* Silicon probe, block-scaled FP4: out[M][N] = sum_k A[m][k] sA[m][k / V] * B[n][k] sB[n][k / V] by the
+ * tensor core's tcgen05.mma kind::mxf4nvf4 (fp32 accumulator, K issued 64 at a time in order).
+ * a [M][K/2] and b [N][K/2] are packed E2M1 codes (element 2i in the low nibble, 16-byte aligned);
+ * sfa [M][K/V] and sfb [N][K/V] are scale bytes: scale_fmt 0 = UE4M3 with V = 16 (NVFP4),
+ * 1 = E8M0 with V = 32 (MXFP4). K must be a multiple of 64. *status as for tc_probe_mma_fp8. */
+int tc_probe_mma_fp4(const uint8_t *a, const uint8_t *b, const uint8_t *sfa, const uint8_t *sfb, int64_t M, int64_t N,
+                     int64_t K, int32_t scale_fmt, float *out, int32_t *status, tc_stream stream);
+
 /* Library version string. */
 const char *tc_version(void);
 
