@@ -139,10 +139,10 @@ def scale_values(codes: torch.Tensor, scale_fmt: int) -> torch.Tensor:
     return torch.ldexp(torch.ones(codes.shape, dtype=torch.float32, device=codes.device), codes.to(torch.int32) - 127)
 
 
-def random_fp4(rows: int, K: int, scale_fmt: int, dist: str, gen: torch.Generator):
+def random_fp4(rows: int, K: int, scale_fmt: int, dist: str, gen: torch.Generator, e8m0_span: int = 30):
     """Seeded E2M1 codes and scale codes. ``"gauss"``: codes of N(0, 2) rounded to the E2M1 grid, scales
     within 2^-3 .. 2^3; ``"codes"``: uniform codes, scales over a wide range (UE4M3: every finite
-    non-zero code; E8M0: 2^-30 .. 2^30)."""
+    non-zero code; E8M0: 2^-e8m0_span .. 2^e8m0_span)."""
     V = FP4_BLOCK[scale_fmt]
     if dist == "gauss":
         x = torch.randn(rows, K, generator=gen) * 2
@@ -157,7 +157,7 @@ def random_fp4(rows: int, K: int, scale_fmt: int, dist: str, gen: torch.Generato
         if scale_fmt == 0:
             sc = torch.randint(1, 0x7F, (rows, K // V), generator=gen)
         else:
-            sc = torch.randint(97, 158, (rows, K // V), generator=gen)
+            sc = torch.randint(127 - e8m0_span, 128 + e8m0_span, (rows, K // V), generator=gen)
     else:
         raise ValueError(f"unknown distribution {dist!r}")
     return codes.to(torch.uint8), sc.to(torch.uint8)
@@ -181,15 +181,16 @@ def candidate_specs_fp4() -> dict[str, MMASpec]:
 
 
 def match_table_fp4(M: int = 256, N: int = 128, K: int = 1024, *, scale_fmt: int = 0, dist: str = "gauss",
-                    seed: int = 0, specs: dict[str, MMASpec] | None = None, device="cuda") -> dict:
+                    seed: int = 0, specs: dict[str, MMASpec] | None = None, device="cuda",
+                    e8m0_span: int = 30) -> dict:
     """``match_table`` for the block-scaled FP4 MMA: each candidate model on the same E2M1 codes and
     per-block scales (the operands TriCast builds for NVFP4 / MXFP4 weights and activations)."""
     from .formats import get_format as fmt_of
 
     V = FP4_BLOCK[scale_fmt]
     gen = torch.Generator().manual_seed(seed)
-    ac, sa = random_fp4(M, K, scale_fmt, dist, gen)
-    bc, sb = random_fp4(N, K, scale_fmt, dist, gen)
+    ac, sa = random_fp4(M, K, scale_fmt, dist, gen, e8m0_span)
+    bc, sb = random_fp4(N, K, scale_fmt, dist, gen, e8m0_span)
     ac, sa, bc, sb = (t.to(device) for t in (ac, sa, bc, sb))
     native = native_mma_fp4(ac, bc, sa, sb, scale_fmt)
     nbits = native.view(torch.int32)
@@ -208,7 +209,10 @@ def match_table_fp4(M: int = 256, N: int = 128, K: int = 1024, *, scale_fmt: int
         ulp = torch.ldexp(torch.ones_like(native, dtype=torch.float64), (torch.frexp(native)[1] - 24).clamp_min(-149))
         diff = ((emu.double() - native.double()).abs() / ulp).nan_to_num(0.0).max()
         rows[name] = {"match": round(float(same.double().mean()), 6), "max_ulp": round(float(diff), 3)}
-    return {"M": M, "N": N, "K": K, "scale": sfmt.name, "block": V, "dist": dist, "seed": seed, "results": rows}
+    table = {"M": M, "N": N, "K": K, "scale": sfmt.name, "block": V, "dist": dist, "seed": seed, "results": rows}
+    if scale_fmt == 1 and dist == "codes":
+        table["e8m0_span"] = e8m0_span
+    return table
 
 
 def main() -> None:
