@@ -48,6 +48,54 @@ struct Stage {
   int2 btw[kN];
 };
 
+// The exact two-pass tile step for one output whose tile failed the single-pass bounds (rare). Called
+// by the whole warp (the TMEM loads are warp-collective); lanes with j < 0 only take part in the loads.
+template <int NG, bool RNE>
+__device__ __noinline__ float exact_tile_step(const fp4::GemmArgs &g, uint32_t buf_addr, int j, float cj, int64_t t,
+                                              int64_t m, int64_t ncol0) {
+  int dj[NG];
+#pragma unroll
+  for (int gg = 0; gg < NG; ++gg) {
+    int v = 0;
+#pragma unroll
+    for (int h = 0; h < kCols / 8; ++h) {
+      uint32_t d[8];
+      tc5::tmem_ld8(buf_addr + (uint32_t)(gg * kN + h * 8), d);
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) v = h * 8 + jj == j ? (int)d[jj] : v;
+    }
+    dj[gg] = v;
+  }
+  if (j < 0) return cj;
+  const int64_t n = ncol0 + j;
+  int emax = fp4::running_exp(cj);
+#pragma unroll
+  for (int gg = 0; gg < NG; ++gg) {
+    const int64_t grow = t * NG + gg;
+    if (dj[gg] == 0) continue;
+    const int label = fp4::exp_class_max(g.am[grow * g.a_rows_pad + m], g.bm[grow * g.b_rows_pad + n]) +
+                      fp4::scale_exp(g.as[grow * g.a_rows_pad + m]) + fp4::scale_exp(g.bs[grow * g.b_rows_pad + n]);
+    emax = max(emax, label);
+  }
+  int64_t total = fp4::running_term(cj, g.F, emax);
+#pragma unroll
+  for (int gg = 0; gg < NG; ++gg) {
+    const int64_t grow = t * NG + gg;
+    const int d = dj[gg];
+    const uint32_t sa = g.as[grow * g.a_rows_pad + m], sb = g.bs[grow * g.b_rows_pad + n];
+    const uint32_t x = (uint32_t)(d < 0 ? -d : d) * (((sa >> 16) & 0xFFu) * ((sb >> 16) & 0xFFu));
+    const int sh = g.shift0 + fp4::scale_exp(sa) + fp4::scale_exp(sb) - emax;
+    // x < 2**20 and sh <= shift0 <= 40: (x << 40) >> (40 - sh) is the exact truncation.
+    const int rs = max(40 - sh, 0);  // sh > 40 only for d == 0 (x == 0)
+    const uint64_t v = rs >= 64 ? 0ull : (((uint64_t)x << 40) >> rs);
+    const bool neg = (d < 0) != (((sa ^ sb) >> 24) & 1u);
+    total += neg ? -(int64_t)v : (int64_t)v;
+  }
+  const uint32_t cb = f2u(cj) & 0x7FFFFFFFu;
+  if (cb < kInf && emax != fp4::kNone) cj = fixed_to_fp32(total, emax, g.F, RNE, true);
+  return cj;
+}
+
 template <int NG, bool RNE>
 __global__ void __launch_bounds__(kThreads, 1) gdfs_fp4_tc_kernel(const __grid_constant__ fp4::GemmArgs g) {
   if (*g.flag) return;  // an operand the encoder rejected: the generic kernel takes over
@@ -149,90 +197,60 @@ __global__ void __launch_bounds__(kThreads, 1) gdfs_fp4_tc_kernel(const __grid_c
       }
       tc5::fence_after_sync();
       const Stage<NG> &st = stages[s];
-      int64_t acc[kCols];
-#pragma unroll
-      for (int j = 0; j < kCols; ++j) acc[j] = 0;
-#pragma unroll
-      for (int gg = 0; gg < NG; ++gg) {
-        uint32_t d[kCols];
-        tc5::tmem_ld16(lane_addr + (uint32_t)((b * NG + gg) * kN), d);
-        const int ma = st.amul[gg][row];
-#pragma unroll
-        for (int j = 0; j < kCols; ++j) acc[j] += (int64_t)(int)d[j] * (int64_t)(ma * st.bmul[gg][col0 + j]);
-      }
-      // Tile step (the tiled kernel's bounds, per output): single pass or the exact fallback.
+      // Tile step (the tiled kernel's bounds, per output): single pass or the exact fallback. Eight
+      // columns at a time, so that the int64 sums fit the 96 registers a thread has (17 warps: five
+      // share one sub-partition's register file) without spilling.
       const int2 wa = st.atw[row];
       uint32_t unsafe = 0;
 #pragma unroll
-      for (int j = 0; j < kCols; ++j) {
-        const int2 wb = st.btw[col0 + j];
-        const uint32_t cb = f2u(c[j]) & 0x7FFFFFFFu;
-        const int be = (int)(cb >> 23);
-        const int lo = max(wa.y + wb.y - (g.F - 23) + 127, 1);
-        const int hi = wa.x + wb.x + g.F - g.srad2 + 127;
-        const bool safe = (wa.x - wa.y) + (wb.x - wb.y) >= g.srad2 - g.F &&
-                          ((cb == 0) | (cb >= kInf) | ((be >= lo) & (be <= hi)));
-        if (safe) {
-          // c + acc * 2**(min es_a + min es_b - srad - 2), exact in fp64 (the clamp only matters for an
-          // all-zero row or column, whose acc is 0).
-          const int e2 = min(max(wa.x + wb.x - g.srad2, -1000), 1000);
-          const double p2 = __hiloint2double((e2 + 1023) << 20, 0);
-          const double v = __fma_rn((double)acc[j], p2, (double)c[j]);
-          float r = (RNE && fabs(v) >= 0x1p-126) ? __double2float_rn(v) : __double2float_rz(v);
-          r = fabs(v) >= 0x1p128 ? __int_as_float((int)((f2u(r) & 0x80000000u) | kInf)) : r;
-          c[j] = cb >= kInf ? c[j] : r;  // an Inf / NaN running value is sticky
-        } else {
-          unsafe |= 1u << j;
+      for (int h = 0; h < kCols / 8; ++h) {
+        int64_t acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0;
+#pragma unroll
+        for (int gg = 0; gg < NG; ++gg) {
+          uint32_t d[8];
+          tc5::tmem_ld8(lane_addr + (uint32_t)((b * NG + gg) * kN + h * 8), d);
+          const int ma = st.amul[gg][row];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] += (int64_t)(int)d[j] * (int64_t)(ma * st.bmul[gg][col0 + h * 8 + j]);
+        }
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const int j = h * 8 + jj;
+          const int2 wb = st.btw[col0 + j];
+          const uint32_t cb = f2u(c[j]) & 0x7FFFFFFFu;
+          const int be = (int)(cb >> 23);
+          const int lo = max(wa.y + wb.y - (g.F - 23) + 127, 1);
+          const int hi = wa.x + wb.x + g.F - g.srad2 + 127;
+          const bool safe = (wa.x - wa.y) + (wb.x - wb.y) >= g.srad2 - g.F &&
+                            ((cb == 0) | (cb >= kInf) | ((be >= lo) & (be <= hi)));
+          if (safe) {
+            // c + acc * 2**(min es_a + min es_b - srad - 2), exact in fp64 (the clamp only matters for an
+            // all-zero row or column, whose acc is 0).
+            const int e2 = min(max(wa.x + wb.x - g.srad2, -1000), 1000);
+            const double p2 = __hiloint2double((e2 + 1023) << 20, 0);
+            const double v = __fma_rn((double)acc[jj], p2, (double)c[j]);
+            float r = (RNE && fabs(v) >= 0x1p-126) ? __double2float_rn(v) : __double2float_rz(v);
+            r = fabs(v) >= 0x1p128 ? __int_as_float((int)((f2u(r) & 0x80000000u) | kInf)) : r;
+            c[j] = cb >= kInf ? c[j] : r;  // an Inf / NaN running value is sticky
+          } else {
+            unsafe |= 1u << j;
+          }
         }
       }
       // Exact two-pass tile step for the outputs that failed the bounds (rare): each round, every lane
-      // takes its lowest pending column; the warp reloads the group sums together.
+      // takes its lowest pending column and the warp runs the step together. It is a separate
+      // (non-inlined) function so that its registers do not count against this loop's.
       while (__any_sync(0xFFFFFFFFu, unsafe != 0)) {
         const int j = unsafe ? __ffs(unsafe) - 1 : -1;
-        int dj[NG];
+        float cj = 0.0f;
 #pragma unroll
-        for (int gg = 0; gg < NG; ++gg) {
-          uint32_t d[kCols];
-          tc5::tmem_ld16(lane_addr + (uint32_t)((b * NG + gg) * kN), d);
-          int v = 0;
+        for (int jj = 0; jj < kCols; ++jj) cj = jj == j ? c[jj] : cj;
+        cj = exact_tile_step<NG, RNE>(g, lane_addr + (uint32_t)(b * NG * kN), j, cj, t, m, n0 + col0);
+        if (j >= 0) unsafe &= unsafe - 1;
 #pragma unroll
-          for (int jj = 0; jj < kCols; ++jj) v = jj == j ? (int)d[jj] : v;
-          dj[gg] = v;
-        }
-        if (j >= 0) {
-          unsafe &= unsafe - 1;
-          const int64_t n = n0 + col0 + j;
-          float cj = 0.0f;
-#pragma unroll
-          for (int jj = 0; jj < kCols; ++jj) cj = jj == j ? c[jj] : cj;
-          int emax = fp4::running_exp(cj);
-#pragma unroll
-          for (int gg = 0; gg < NG; ++gg) {
-            const int64_t grow = t * NG + gg;
-            if (dj[gg] == 0) continue;
-            const int label = fp4::exp_class_max(g.am[grow * g.a_rows_pad + m], g.bm[grow * g.b_rows_pad + n]) +
-                              fp4::scale_exp(g.as[grow * g.a_rows_pad + m]) + fp4::scale_exp(g.bs[grow * g.b_rows_pad + n]);
-            emax = max(emax, label);
-          }
-          int64_t total = fp4::running_term(cj, g.F, emax);
-#pragma unroll
-          for (int gg = 0; gg < NG; ++gg) {
-            const int64_t grow = t * NG + gg;
-            const int d = dj[gg];
-            const uint32_t sa = g.as[grow * g.a_rows_pad + m], sb = g.bs[grow * g.b_rows_pad + n];
-            const uint32_t x = (uint32_t)(d < 0 ? -d : d) * (((sa >> 16) & 0xFFu) * ((sb >> 16) & 0xFFu));
-            const int sh = g.shift0 + fp4::scale_exp(sa) + fp4::scale_exp(sb) - emax;
-            // x < 2**20 and sh <= shift0 <= 40: (x << 40) >> (40 - sh) is the exact truncation.
-            const int rs = max(40 - sh, 0);  // sh > 40 only for d == 0 (x == 0)
-            const uint64_t v = rs >= 64 ? 0ull : (((uint64_t)x << 40) >> rs);
-            const bool neg = (d < 0) != (((sa ^ sb) >> 24) & 1u);
-            total += neg ? -(int64_t)v : (int64_t)v;
-          }
-          const uint32_t cb = f2u(cj) & 0x7FFFFFFFu;
-          if (cb < kInf && emax != fp4::kNone) cj = fixed_to_fp32(total, emax, g.F, RNE, true);
-#pragma unroll
-          for (int jj = 0; jj < kCols; ++jj) c[jj] = jj == j ? cj : c[jj];
-        }
+        for (int jj = 0; jj < kCols; ++jj) c[jj] = jj == j ? cj : c[jj];
       }
       tc5::fence_before_sync();
       __syncwarp();
