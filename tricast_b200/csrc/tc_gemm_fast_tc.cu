@@ -197,27 +197,27 @@ __global__ void __launch_bounds__(kThreads, 1) gdfs_fp4_tc_kernel(const __grid_c
       }
       tc5::fence_after_sync();
       const Stage<NG> &st = stages[s];
-      // Tile step (the tiled kernel's bounds, per output): single pass or the exact fallback. Eight
+      // Tile step (the tiled kernel's bounds, per output): single pass or the exact fallback. Four
       // columns at a time, so that the int64 sums fit the 96 registers a thread has (17 warps: five
       // share one sub-partition's register file) without spilling.
       const int2 wa = st.atw[row];
       uint32_t unsafe = 0;
 #pragma unroll
-      for (int h = 0; h < kCols / 8; ++h) {
-        int64_t acc[8];
+      for (int h = 0; h < kCols / 4; ++h) {
+        int64_t acc[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = 0;
+        for (int j = 0; j < 4; ++j) acc[j] = 0;
 #pragma unroll
         for (int gg = 0; gg < NG; ++gg) {
-          uint32_t d[8];
-          tc5::tmem_ld8(lane_addr + (uint32_t)((b * NG + gg) * kN + h * 8), d);
+          uint32_t d[4];
+          tc5::tmem_ld4(lane_addr + (uint32_t)((b * NG + gg) * kN + h * 4), d);
           const int ma = st.amul[gg][row];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j] += (int64_t)(int)d[j] * (int64_t)(ma * st.bmul[gg][col0 + h * 8 + j]);
+          for (int j = 0; j < 4; ++j) acc[j] += (int64_t)(int)d[j] * (int64_t)(ma * st.bmul[gg][col0 + h * 4 + j]);
         }
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          const int j = h * 8 + jj;
+        for (int jj = 0; jj < 4; ++jj) {
+          const int j = h * 4 + jj;
           const int2 wb = st.btw[col0 + j];
           const uint32_t cb = f2u(c[j]) & 0x7FFFFFFFu;
           const int be = (int)(cb >> 23);
@@ -225,18 +225,16 @@ __global__ void __launch_bounds__(kThreads, 1) gdfs_fp4_tc_kernel(const __grid_c
           const int hi = wa.x + wb.x + g.F - g.srad2 + 127;
           const bool safe = (wa.x - wa.y) + (wb.x - wb.y) >= g.srad2 - g.F &&
                             ((cb == 0) | (cb >= kInf) | ((be >= lo) & (be <= hi)));
-          if (safe) {
-            // c + acc * 2**(min es_a + min es_b - srad - 2), exact in fp64 (the clamp only matters for an
-            // all-zero row or column, whose acc is 0).
-            const int e2 = min(max(wa.x + wb.x - g.srad2, -1000), 1000);
-            const double p2 = __hiloint2double((e2 + 1023) << 20, 0);
-            const double v = __fma_rn((double)acc[jj], p2, (double)c[j]);
-            float r = (RNE && fabs(v) >= 0x1p-126) ? __double2float_rn(v) : __double2float_rz(v);
-            r = fabs(v) >= 0x1p128 ? __int_as_float((int)((f2u(r) & 0x80000000u) | kInf)) : r;
-            c[j] = cb >= kInf ? c[j] : r;  // an Inf / NaN running value is sticky
-          } else {
-            unsafe |= 1u << j;
-          }
+          // c + acc * 2**(min es_a + min es_b - srad - 2), exact in fp64 (the clamp only matters for an
+          // all-zero row or column, whose acc is 0). Computed for every output and kept only where the
+          // bounds hold (no branch: the unsafe outputs are rare and redone below).
+          const int e2 = min(max(wa.x + wb.x - g.srad2, -1000), 1000);
+          const double p2 = __hiloint2double((e2 + 1023) << 20, 0);
+          const double v = __fma_rn((double)acc[jj], p2, (double)c[j]);
+          float r = (RNE && fabs(v) >= 0x1p-126) ? __double2float_rn(v) : __double2float_rz(v);
+          r = fabs(v) >= 0x1p128 ? __int_as_float((int)((f2u(r) & 0x80000000u) | kInf)) : r;
+          c[j] = (safe && cb < kInf) ? r : c[j];  // an Inf / NaN running value is sticky
+          unsafe |= safe ? 0u : 1u << j;
         }
       }
       // Exact two-pass tile step for the outputs that failed the bounds (rare): each round, every lane
