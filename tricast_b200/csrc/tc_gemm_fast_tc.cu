@@ -35,6 +35,7 @@ constexpr int kN = 64;   // columns of B per CTA
 constexpr int kStages = 4;
 constexpr int kEpiWarps = 16;
 constexpr int kCols = kN / (kEpiWarps / 4);  // columns per epilogue thread
+constexpr int kChunk = 4;                    // columns per tile-step pass (bounds the live int64 sums)
 constexpr int kThreads = (kEpiWarps + 1) * 32;
 constexpr uint32_t kTmemCols = 512;  // two buffers of NG (<= 4) groups x 64 columns
 
@@ -197,27 +198,27 @@ __global__ void __launch_bounds__(kThreads, 1) gdfs_fp4_tc_kernel(const __grid_c
       }
       tc5::fence_after_sync();
       const Stage<NG> &st = stages[s];
-      // Tile step (the tiled kernel's bounds, per output): single pass or the exact fallback. Four
+      // Tile step (the tiled kernel's bounds, per output): single pass or the exact fallback. kChunk
       // columns at a time, so that the int64 sums fit the 96 registers a thread has (17 warps: five
       // share one sub-partition's register file) without spilling.
       const int2 wa = st.atw[row];
       uint32_t unsafe = 0;
 #pragma unroll
-      for (int h = 0; h < kCols / 4; ++h) {
-        int64_t acc[4];
+      for (int h = 0; h < kCols / kChunk; ++h) {
+        int64_t acc[kChunk];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[j] = 0;
+        for (int j = 0; j < kChunk; ++j) acc[j] = 0;
 #pragma unroll
         for (int gg = 0; gg < NG; ++gg) {
-          uint32_t d[4];
-          tc5::tmem_ld4(lane_addr + (uint32_t)((b * NG + gg) * kN + h * 4), d);
+          uint32_t d[kChunk];
+          tc5::tmem_ld<kChunk>(lane_addr + (uint32_t)((b * NG + gg) * kN + h * kChunk), d);
           const int ma = st.amul[gg][row];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) acc[j] += (int64_t)(int)d[j] * (int64_t)(ma * st.bmul[gg][col0 + h * 4 + j]);
+          for (int j = 0; j < kChunk; ++j) acc[j] += (int64_t)(int)d[j] * (int64_t)(ma * st.bmul[gg][col0 + h * kChunk + j]);
         }
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const int j = h * 4 + jj;
+        for (int jj = 0; jj < kChunk; ++jj) {
+          const int j = h * kChunk + jj;
           const int2 wb = st.btw[col0 + j];
           const uint32_t cb = f2u(c[j]) & 0x7FFFFFFFu;
           const int be = (int)(cb >> 23);

@@ -93,5 +93,14 @@ __device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// N (4, 8 or 16) consecutive 32-bit TMEM columns of this thread's lane (warp-collective), then wait.
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
+  static_assert(N == 4 || N == 8 || N == 16, "tmem_ld: 4, 8 or 16 columns");
+  if constexpr (N == 4) tmem_ld4(taddr, r);
+  else if constexpr (N == 8) tmem_ld8(taddr, r);
+  else tmem_ld16(taddr, r);
+}
+
 }  // namespace tc5
 }  // namespace tc
