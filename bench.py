@@ -106,10 +106,11 @@ def measure_cfg1(dev, steps: int, warmup: int) -> dict:
             "copy_same_protocol_ms": tc}
 
 
-def measure_gemm_config(dev, name: str, steps: int, warmup: int) -> dict:
+def measure_gemm_config(dev, name: str, steps: int, warmup: int, size: int = 0) -> dict:
     """Device-resident step of cfg3 (FP8 E4M3 W8A8, Hopper CoFDA F=13 CS=32, 8192^3) or cfg4
     (INT8 per-token x INT4 g128 asymmetric, CoFDA F=23 promoted every 128, 4096x12288x4096):
-    quantize both operands + emulated GEMM, L2 flushed between steps, CUDA-event timed."""
+    quantize both operands + emulated GEMM, L2 flushed between steps, CUDA-event timed. ``size``
+    (cfg3 only, profiling) replaces 8192 by a smaller cube."""
     import torch
 
     from tricast_b200 import as_operand, gemm_triton, quantize_triton
@@ -119,7 +120,7 @@ def measure_gemm_config(dev, name: str, steps: int, warmup: int) -> dict:
 
     g = torch.Generator().manual_seed(0)
     if name == "cfg3":
-        m, n, k = 8192, 8192, 8192
+        m = n = k = size or 8192
         a = torch.randn(m, k, generator=g).bfloat16().to(dev)
         b = (torch.randn(n, k, generator=g) * 0.02).bfloat16().to(dev)
         spec = PRESETS["nvidia_hopper_fp8"].with_(out_format="fp32")
@@ -543,6 +544,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg2step", "cfg1", "cfg3", "cfg4", "decode"],
                     help="cfg2step/cfg1/cfg3/cfg4/decode run only that measurement (for profiling)")
+    ap.add_argument("--cube", type=int, default=0,
+                    help="with --workload cfg3: run an M = N = K = CUBE case instead of 8192 (profiling)")
     args = ap.parse_args()
     if args.workload != "cfg2" and args.impl != "reference":
         import torch
@@ -555,7 +558,7 @@ def main() -> None:
         elif args.workload == "decode":
             print(json.dumps(measure_decode(dev, calls=args.steps)))
         else:
-            print(json.dumps(measure_gemm_config(dev, args.workload, args.steps, args.warmup)))
+            print(json.dumps(measure_gemm_config(dev, args.workload, args.steps, args.warmup, args.cube)))
         return
     if args.impl == "reference":
         run_reference(args)
