@@ -97,6 +97,26 @@ struct Acc<float> {
     if (field < 1 || field > 254) return fixed_to_fp32((int64_t)tot, emax, F, rne, true);
     return u2f(((uint32_t)field << 23) | (r & 0x7FFFFFu) | (f2u(tot) & 0x80000000u));
   }
+  // Branch-free forms for the per-output steps of a chunk: the common case is computed with selects
+  // and `rare` reports an output that needs the general routine above (running: F - emax > 127;
+  // finish: a result outside the normal range), which the caller redoes for the few that set it.
+  static __device__ __forceinline__ float running_fast(float c, float s, int F, int emax, bool &rare) {
+    const uint32_t a = f2u(c) & 0x7FFFFFFFu;
+    const bool live = (a != 0) & (a < kInf);
+    rare = live & (F - emax > 127);
+    const float t = trunc_scaled(c, s);
+    return live ? t : 0.0f;
+  }
+  static __device__ __forceinline__ float finish_fast(float tot, int emax, int F, bool rne, bool &rare) {
+    const uint32_t a = f2u(tot) & 0x7FFFFFFFu;
+    const int drop = F < 23 ? 23 - F : 0;
+    const uint32_t up = (rne && drop > 0) ? ((1u << drop) >> 1) - 1u + ((a >> drop) & 1u) : 0u;
+    const uint32_t r = (a + up) & ~((1u << drop) - 1u);
+    const int field = (int)(r >> 23) + emax - F;
+    rare = (a != 0) & ((field < 1) | (field > 254));
+    const float v = u2f(((uint32_t)field << 23) | (r & 0x7FFFFFu) | (f2u(tot) & 0x80000000u));
+    return a == 0 ? 0.0f : v;
+  }
 };
 
 template <>
@@ -129,6 +149,22 @@ struct Acc<double> {
     const int field = (int)(r >> 52) - 1023 + 127 + emax - F;
     if (field < 1 || field > 254) return fixed_to_fp32((int64_t)tot, emax, F, rne, true);
     return u2f(((uint32_t)field << 23) | (uint32_t)((r >> 29) & 0x7FFFFFu) | (uint32_t)(bits >> 32 & 0x80000000u));
+  }
+  // Branch-free forms, as for fp32 (the fp64 running term has no rare case).
+  static __device__ __forceinline__ double running_fast(float c, double s, int F, int emax, bool &rare) {
+    rare = false;
+    return running(c, F, emax, s);
+  }
+  static __device__ __forceinline__ float finish_fast(double tot, int emax, int F, bool rne, bool &rare) {
+    const uint64_t bits = (uint64_t)__double_as_longlong(tot);
+    const uint64_t a = bits & 0x7FFFFFFFFFFFFFFFull;
+    const int drop = 52 - (F < 23 ? F : 23);
+    const uint64_t up = rne ? ((1ull << drop) >> 1) - 1ull + ((a >> drop) & 1ull) : 0ull;
+    const uint64_t r = (a + up) & ~((1ull << drop) - 1ull);
+    const int field = (int)(r >> 52) - 1023 + 127 + emax - F;
+    rare = (a != 0) & ((field < 1) | (field > 254));
+    const float v = u2f(((uint32_t)field << 23) | (uint32_t)((r >> 29) & 0x7FFFFFu) | (uint32_t)(bits >> 32 & 0x80000000u));
+    return a == 0 ? 0.0f : v;
   }
 };
 
