@@ -34,9 +34,10 @@ M, N, K = 2048, 4096, 4096
 WORKLOAD = ("cfg2 NVFP4 W4A4 emulated GEMM 2048x4096x4096: quantize A,B (nvfp4) + Blackwell-FP4 GDFS "
             "(G=6,F=35,GS=16,KT=64) fp32 out")
 L2_FLUSH_BYTES = 512 << 20
-# dram__bytes_read.sum + dram__bytes_write.sum of one gdfs_fp4_kernel<4> launch on cfg2 (one ncu
-# --set full capture of this bench's first timed step).
-GDFS_TRAFFIC_BYTES = 40_644_352 + 3_510_272
+# dram__bytes_read.sum + dram__bytes_write.sum of one gdfs_fp4_tc_kernel<4, 0> launch on cfg2 (the ncu
+# capture summarised in profiles/gdfs_fp4_tc_kernel_cfg2.md).
+GDFS_TRAFFIC_BYTES = 40_630_784 + 2_835_968
+GDFS_ISSUE_UTIL = 0.599  # smsp__issue_active.avg.pct_of_peak_sustained_active / 100, same capture
 
 
 CFG1_BYTES_PER_ELEM = 4 + 4 + 0.5 + 1 / 32  # fp32 in, fp32 dequant out, E2M1 nibble, E8M0 byte per 32
@@ -510,11 +511,13 @@ def run_b200(args) -> None:
             "gpu_launches": int(launches),
             "roofline": {"bound": "alu", "achieved": achieved, "peak": peak_gmacs, "unit": "GMAC/s",
                          "frac": achieved / peak_gmacs, "traffic": GDFS_TRAFFIC_BYTES,
+                         "issue_util": GDFS_ISSUE_UTIL,
                          "note": f"emulated GEMM (encode + GDFS kernel, CUDA events); the group dot products "
                                  "run on tcgen05 int8 MMAs and the exact int64/fp64 tile arithmetic on the CUDA "
                                  f"cores bounds the kernel; peak = the CUDA-core DP4A rate, 148 SMs x {dp4a_lanes} "
                                  f"lanes x 4 MAC x {sm_mhz:.0f} MHz; traffic = DRAM bytes per GDFS launch from one "
-                                 "ncu capture"},
+                                 "ncu capture; issue_util = smsp__issue_active of that capture (the issue-slot "
+                                 "share the kernel keeps busy)"},
             "gemm_ms": t_gemm,
             "aux_sweep": {"workload": "cfg5 per-layer error sweep: 196 Qwen3-0.6B-shaped layers x "
                                       "(MXFP4, NVFP4, FP8 E4M3, INT4-g128) vs fp64, 2048 tokens",
