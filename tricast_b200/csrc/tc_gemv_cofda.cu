@@ -108,30 +108,23 @@ __global__ void __launch_bounds__(256) prep_a_kernel(PrepArgs e) {
 // One B element: value with its folded scale (exponent s_exp, or zero) and exponent label. A value
 // the fast path cannot take sets bad (its outputs are then recomputed by the exact kernel).
 __device__ __forceinline__ void decode_b(float x, const Fmt &f, int s_exp, bool s_zero, float &v, int &e, bool &bad) {
+  // Branch-free: every test is evaluated and folded into `bad` (a rejected element sends the whole
+  // product to the exact kernel, so its value and label do not matter). Zero elements and elements
+  // under a zero K scale are zero product terms; fp32 subnormals (below every narrow grid), NaN / Inf,
+  // off-grid values, exponents beyond the format and folded exponents outside [-50, 60] are rejected.
   const uint32_t u = f2u(x), a = u & 0x7FFFFFFFu;
   const uint32_t field = a >> 23;
-  v = 0.0f;
-  e = cofda::kZeroExp;
-  if (a == 0) return;
-  if (field == 0 || field == 255) {  // fp32 subnormal (below every narrow grid) or NaN / Inf
-    bad = true;
-    return;
-  }
-  if (s_zero) return;  // a zero K scale makes the element a zero product term
   const int fl = (int)field - 127;
   const int ee = fl > f.emin ? fl : f.emin;
   const int sh = 23 - f.mbits + (ee - fl);  // fraction bits below the grid, all zero on the grid
-  if (ee > f.emax || sh > 23 || (a & ((1u << sh) - 1u)) != 0u) {
-    bad = true;
-    return;
-  }
-  e = ee + s_exp;
-  if (e < -50 || e > 60) {
-    bad = true;
-    e = cofda::kZeroExp;
-    return;
-  }
-  v = u2f(u + ((uint32_t)s_exp << 23));  // exact: the folded value stays a normal fp32 number
+  const uint32_t below = sh > 23 ? 0xFFFFFFFFu : (1u << sh) - 1u;
+  const bool nz = a != 0;
+  const bool live = nz & !s_zero;
+  const int ef = ee + s_exp;
+  bad |= nz & ((field == 0) | (field == 255));
+  bad |= live & ((ee > f.emax) | ((a & below) != 0u) | (ef < -50) | (ef > 60));
+  e = live ? ef : cofda::kZeroExp;
+  v = live ? u2f(u + ((uint32_t)s_exp << 23)) : 0.0f;  // exact: the folded value stays a normal fp32 number
 }
 
 template <class T, int N>
