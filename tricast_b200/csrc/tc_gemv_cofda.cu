@@ -456,9 +456,10 @@ static int launch_cofda_gemv_typed(const GemmDesc &g, const CofdaGemvPlan &p, ch
   }
   a.g = g;
   a.flag = flag;
-  // Lanes per output: 8 while few rows leave the GPU short of threads, else 4. Columns per CTA: the
-  // largest power of two whose M x cols slots fit the CTA.
-  const int LG = g.M <= 4 ? 8 : 4;
+  // Lanes per output: 16 for a single row (twice the CTAs of 8 lanes: 256 for N = 4096), 8 while few
+  // rows leave the GPU short of threads, else 4; at least two products per lane and chunk. Columns
+  // per CTA: the largest power of two whose M x cols slots fit the CTA.
+  const int LG = (g.M == 1 && g.CS >= 32) ? 16 : (g.M <= 4 ? 8 : 4);
   const int slots = cgemv::kThreads / LG;
   int cols = 1;
   while (cols * 2 * g.M <= slots) cols *= 2;
@@ -467,6 +468,7 @@ static int launch_cofda_gemv_typed(const GemmDesc &g, const CofdaGemvPlan &p, ch
   int mp = 1;
   while (mp < g.M) mp *= 2;
   a.KC = (sizeof(T) == 4 ? 4096 : 2048) / std::max(cols, mp);
+  if (LG == 16) return launch_cofda_gemv_t<32, 16, T>(a, s);
   return LG == 8 ? launch_cofda_gemv_cs<8, T>(a, g.CS, s) : launch_cofda_gemv_cs<4, T>(a, g.CS, s);
 }
 
