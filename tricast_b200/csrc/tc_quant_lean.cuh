@@ -293,7 +293,7 @@ __global__ void __launch_bounds__(256, 4) group_lean_kernel(const LeanArgs a) {
                            : reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.x) + off);
 #pragma unroll
     for (int k = 0; k < E / 4; ++k)
-      if (x32 || k < E / 8) raw[k] = src[k];
+      if (x32 || k < E / 8) raw[k] = __ldcs(src + k);  // read once: evict-first (measured 33.7 -> 32.7 us on cfg1)
   };
   int64_t base = warp * kGroupsPerWarp;
   fetch(base + lane / LG);
