@@ -85,21 +85,40 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t c) {
 //     input, which rejects everything else (other fraction bits, other exponents, NaN, Inf, 0.75);
 //   * signs become byte masks by sign-replicating permutes, and a negative code is (m ^ 0xFF) + 1
 //     per byte (no carry: m >= 1 where the mask is set).
-// orm collects the magnitudes: bit 3 of a byte marks |v| >= 4, bits 2..3 |v| >= 2.
-__device__ __forceinline__ uint32_t e2m1_codes4_bf16(uint32_t w0, uint32_t w1, bool &ok, uint32_t &orm) {
+// mag returns the four code magnitudes |2v|, one byte each: bit 3 of a byte marks |v| >= 4, bits
+// 2..3 |v| >= 2. e2m1_codes4_bf16 collects them into orm across calls.
+__device__ __forceinline__ uint32_t e2m1_codes4_bf16_mag(uint32_t w0, uint32_t w1, bool &ok, uint32_t &mag) {
   const uint32_t x0 = w0 & 0x7FFF7FFFu, x1 = w1 & 0x7FFF7FFFu;
   const uint32_t nz = prmt(x0 + 0x7FFF7FFFu, x1 + 0x7FFF7FFFu, 0xFDB9u);
   const uint32_t t0 = (w0 >> 6) & 0x00070007u, t1 = (w1 >> 6) & 0x00070007u;
   const uint32_t sel = ((t0 | (t0 >> 12)) & 0xFFu) | (((t1 | (t1 >> 12)) & 0xFFu) << 8);
-  const uint32_t mag = prmt(0x0C080604u, 0x03020001u, sel) & nz;
+  mag = prmt(0x0C080604u, 0x03020001u, sel) & nz;
   const uint32_t live8 = mag + 0x7F7F7F7Fu;  // bit 7 of byte k: element k has a code
   const uint32_t lo = prmt(0xC0804000u, 0xC0804000u, sel), hi = prmt(0x40404040u, 0x3F3F3F3Fu, sel);
   const uint32_t r0 = prmt(lo, hi, 0x5140u) & prmt(live8, live8, 0x9988u);
   const uint32_t r1 = prmt(lo, hi, 0x7362u) & prmt(live8, live8, 0xBBAAu);
   ok &= (r0 == x0) & (r1 == x1);
   const uint32_t smask = prmt(w0, w1, 0xFDB9u) & prmt(live8, live8, 0xBA98u);
-  orm |= mag;
   return (mag ^ smask) + (smask & 0x01010101u);
+}
+
+__device__ __forceinline__ uint32_t e2m1_codes4_bf16(uint32_t w0, uint32_t w1, bool &ok, uint32_t &orm) {
+  uint32_t mag;
+  const uint32_t codes = e2m1_codes4_bf16_mag(w0, w1, ok, mag);
+  orm |= mag;
+  return codes;
+}
+
+// Bit 7 of byte k of x to bit k (k = 0..3): the four terms of the product land on distinct bits
+// below bit 28 or on bits 28..31, so no carry reaches the result.
+__device__ __forceinline__ uint32_t byte_msb4(uint32_t x) { return ((x & 0x80808080u) * 0x00204081u) >> 28; }
+
+// The exponent-class masks of four elements from their code magnitudes (bytes of 2|v|, at most 12):
+// c0 non-zero, c1 |v| >= 2 (magnitude >= 4), c2 |v| >= 4 (magnitude >= 8), one bit per element.
+__device__ __forceinline__ void class_masks4(uint32_t mag, uint32_t &c0, uint32_t &c1, uint32_t &c2) {
+  c0 = byte_msb4(mag + 0x7F7F7F7Fu);
+  c1 = byte_msb4((mag & 0x0C0C0C0Cu) + 0x7F7F7F7Fu);
+  c2 = byte_msb4((mag & 0x08080808u) << 4);
 }
 
 // A group's K scale as (es, ms, sign) at the scale format's radix, or zero (the group becomes a zero

@@ -64,7 +64,32 @@ __global__ void __launch_bounds__(256) encode_fp4_kernel(EncodeArgs e) {
     uint32_t codes[4] = {0, 0, 0, 0};
     uint32_t c0 = 0, c1 = 0, c2 = 0;     // exponent-class masks: >= 0 (nonzero), >= 1, >= 2
     uint32_t sword = pack_scale(0, 0, 0);
-    if (r < e.rows) {
+    if (r < e.rows && e.vec && k0 + kGS <= e.K && e.dt == TC_BF16) {
+      // Whole group in bf16 containers: codes and exponent-class masks four elements at a time from
+      // the bit patterns (e2m1_codes4_bf16_mag), no float conversion.
+      const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(e.v) + r * e.K + k0);
+      const uint4 u0 = src[0], u1 = src[1];
+      const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      bool ok = true;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t mag, m0, m1, m2;
+        codes[q] = e2m1_codes4_bf16_mag(w[2 * q], w[2 * q + 1], ok, mag);
+        class_masks4(mag, m0, m1, m2);
+        c0 |= m0 << (4 * q);
+        c1 |= m1 << (4 * q);
+        c2 |= m2 << (4 * q);
+      }
+      if (!ok) bad = true;
+      bool zero = false;
+      sword = e.scale ? group_scale_word(e.scale[r * e.nkd + k0 / e.kd], e.sf, e.field0, zero, bad) : pack_scale(0, 1, 0);
+      if (zero) {
+        codes[0] = codes[1] = codes[2] = codes[3] = 0;
+        c0 = c1 = c2 = 0;
+      }
+      const uint32_t gemax = c2 ? 2u : c1 ? 1u : 0u;
+      sword |= (gemax << 25) | ((c0 == 0 ? 1u : 0u) << 27);
+    } else if (r < e.rows) {
       // The group's 16 inputs: vector loads when the whole group is in range and 16-byte aligned.
       float vin[kGS];
       if (e.vec && k0 + kGS <= e.K) {
