@@ -44,7 +44,7 @@ CFG1_BYTES_PER_ELEM = 4 + 4 + 0.5 + 1 / 32  # fp32 in, fp32 dequant out, E2M1 ni
 
 
 def make_cfg1_input():
-    """cfg1: 4096x4096 fp32 N(0,1), 0.1% of entries x50, seed 0."""
+    """cfg1: 4096x4096 fp32 N(0,1), 0.1% of entries x50, seed 0 (the benchmark's MXFP4 cast input)."""
     import torch
 
     g = torch.Generator().manual_seed(0)
@@ -243,7 +243,7 @@ def measure_cfg2_step(dev, steps: int, warmup: int) -> dict:
 
 
 def make_inputs(rank: int):
-    """Seeded CPU generation so every GPU count sees identical tensors."""
+    """cfg2 operands, generated seeded on the CPU so every GPU count sees identical tensors."""
     import torch
 
     g = torch.Generator().manual_seed(0)

@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this folder by running TriCast's own reference backend.
 
-Run once on a machine that has the TriCast checkout (its ``src`` on ``TRICAST_SRC``, default the
-reference mount): ``python tests/golden/make_golden.py``. The fixtures are committed; nothing at
+Run once on a machine that has a TriCast checkout, with ``TRICAST_SRC`` set to its ``src``
+directory: ``TRICAST_SRC=<checkout>/src python tests/golden/make_golden.py``. The fixtures are committed; nothing at
 test time reads the TriCast checkout.
 
 Contents:
@@ -33,7 +33,9 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-SRC = os.environ.get("TRICAST_SRC", "/root/reference/src")
+SRC = os.environ.get("TRICAST_SRC", "")
+if not SRC:
+    sys.exit("set TRICAST_SRC to the src directory of a TriCast checkout")
 sys.path.insert(0, SRC)
 
 from tricast.analysis import error_metrics  # noqa: E402
