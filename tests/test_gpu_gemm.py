@@ -281,6 +281,36 @@ def test_int_promote_fast_path_vs_oracle(shape):
     assert bits_equal(gemm_triton(a8, b8, spec).cpu().numpy(), _oracle_gemm(a8, b8, spec))
 
 
+@pytest.mark.parametrize("scheme", ["nvfp4", "mxfp4"])
+@pytest.mark.parametrize("shape", [(130, 64, 1024), (40, 200, 1000)])
+def test_gdfs_fp4_compact_bf16_operands(scheme, shape):
+    """Operands in bf16 containers (``as_operand(..., compact=True)``, as the benchmark passes them) on
+    the tiled kernel: whole groups are encoded four elements at a time from their bit patterns, and a
+    ragged K leaves the last group to the per-element path. Bit-exact against the oracle with the fast
+    kernel producing the result; a NaN inside a bf16 group must hand the product to the exact kernel,
+    which is bit-exact too."""
+    m, n, k = shape
+    g = torch.Generator().manual_seed(m + n + k)
+    xa = torch.randn(m, k, generator=g)
+    xa[:, torch.randperm(k, generator=g)[:4]] *= 20
+    xb = torch.randn(n, k, generator=g) * 0.02
+    a = as_operand(quantize_triton(xa.bfloat16().cuda(), SCHEMES[scheme]), compact=True)
+    b = as_operand(quantize_triton(xb.bfloat16().cuda(), SCHEMES[scheme]), compact=True)
+    assert a.values.dtype == torch.bfloat16 and b.values.dtype == torch.bfloat16
+    spec = PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32")
+    before = exact_fallbacks()
+    got = gemm_triton(a, b, spec).float().cpu().numpy()
+    assert exact_fallbacks() == before, "the fast kernel declined compact on-grid operands"
+    want = _oracle_gemm(a, b, spec)
+    assert bits_equal(got, want), first_mismatch(got, want)
+    b.values[7, 37] = float("nan")
+    before = exact_fallbacks()
+    got = gemm_triton(a, b, spec).float().cpu().numpy()
+    assert exact_fallbacks() > before, "a NaN element did not reach the exact kernel"
+    want = _oracle_gemm(a, b, spec)
+    assert bits_equal(got, want), first_mismatch(got, want)
+
+
 @pytest.mark.parametrize("rows", [40, 3])  # tiled kernel and small-M kernel
 def test_cofda_tiny_folded_scales(rows):
     """Power-of-two product scales that fold into tiny values: labels down to -50 stay on the fast
