@@ -281,6 +281,25 @@ def test_int_promote_fast_path_vs_oracle(shape):
     assert bits_equal(gemm_triton(a8, b8, spec).cpu().numpy(), _oracle_gemm(a8, b8, spec))
 
 
+@pytest.mark.parametrize("scheme,preset", [("fp8_tensor", "nvidia_hopper_fp8"), ("fp8_tensor", "nvidia_blackwell_fp8"),
+                                           ("mxfp8_e4m3", "nvidia_ada_fp8")])
+def test_cofda_compact_bf16_operands(scheme, preset):
+    """The tiled CoFDA kernel on operands in bf16 containers (as cfg3 passes them), fp32 and fp64
+    accumulation, a ragged K: bit-exact against the oracle, produced by the fast kernel."""
+    g = torch.Generator().manual_seed(7)
+    xa = torch.randn(130, 1000, generator=g)
+    xb = torch.randn(72, 1000, generator=g) * 0.02
+    a = as_operand(quantize_triton(xa.bfloat16().cuda(), SCHEMES[scheme]), compact=True)
+    b = as_operand(quantize_triton(xb.bfloat16().cuda(), SCHEMES[scheme]), compact=True)
+    assert a.values.dtype == torch.bfloat16 and b.values.dtype == torch.bfloat16
+    spec = PRESETS[preset].with_(out_format="fp32")
+    before = exact_fallbacks()
+    got = gemm_triton(a, b, spec).float().cpu().numpy()
+    assert exact_fallbacks() == before, "the fast kernel declined compact on-grid operands"
+    want = _oracle_gemm(a, b, spec)
+    assert bits_equal(got, want), first_mismatch(got, want)
+
+
 @pytest.mark.parametrize("scheme", ["nvfp4", "mxfp4"])
 @pytest.mark.parametrize("shape", [(130, 64, 1024), (40, 200, 1000)])
 def test_gdfs_fp4_compact_bf16_operands(scheme, shape):
