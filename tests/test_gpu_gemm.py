@@ -86,15 +86,17 @@ def test_preset_configs_vs_oracle(scheme, preset, out):
     assert bits_equal(got, want), first_mismatch(got, want)
 
 
-def test_cfg4_mapping_vs_oracle():
-    """INT8 row-scaled activations x INT4 g128 asymmetric weights, CoFDA F=23 promoted every 128."""
+@pytest.mark.parametrize("compact", [False, True])
+def test_cfg4_mapping_vs_oracle(compact):
+    """INT8 row-scaled activations x INT4 g128 asymmetric weights, CoFDA F=23 promoted every 128; the
+    activations also in bf16 containers, as the benchmark passes them."""
     g = torch.Generator().manual_seed(4)
     x = torch.randn(48, 1024, generator=g)
     w = torch.randn(80, 1024, generator=g) * 0.02
     qa = quantize_triton(x.cuda(), SCHEMES["int8_row"])
     qw = quantize_triton(w.cuda(), SCHEMES["int4_g128_zp"])
     z = qw.zero_point.repeat_interleave(128, dim=1)[:, :1024]
-    a = as_operand(qa)
+    a = as_operand(qa, compact=compact)
     b = Operand(qw.values.float() - z, IntFormat("int5", 5), qw.scale, FP16, "k", 128)
     spec = MMASpec("cofda", f_bits=23, chunk_size=32, promote_interval=128, out_format="fp32")
     got = gemm_triton(a, b, spec).cpu().numpy()
@@ -269,7 +271,7 @@ def test_int_promote_fast_path_vs_oracle(shape):
     qa = quantize_triton(torch.randn(m, k, generator=g).cuda(), SCHEMES["int8_row"])
     qw = quantize_triton((torch.randn(n, k, generator=g) * 0.02).cuda(), SCHEMES["int4_g128_zp"])
     z = qw.zero_point.repeat_interleave(128, dim=1)[:, :k]
-    a = as_operand(qa)
+    a = as_operand(qa, compact=compact)
     b = Operand(qw.values.float() - z, IntFormat("int5", 5), qw.scale, FP16, "k", 128)
     spec = MMASpec("cofda", f_bits=23, chunk_size=32, promote_interval=128, out_format="fp32")
     got = gemm_triton(a, b, spec).cpu().numpy()
@@ -386,7 +388,7 @@ def test_int_tensor_core_path(shape):
     qa = quantize_triton(x.cuda(), SCHEMES["int8_row"])
     qw = quantize_triton(w.cuda(), SCHEMES["int4_g128_zp"])
     z = qw.zero_point.repeat_interleave(128, dim=1)[:, :k]
-    a = as_operand(qa)
+    a = as_operand(qa, compact=compact)
     b = Operand(qw.values.float() - z, IntFormat("int5", 5), qw.scale, FP16, "k", 128)
     spec = MMASpec("cofda", f_bits=23, chunk_size=32, promote_interval=128, out_format="fp32")
     before = exact_fallbacks()
