@@ -271,7 +271,7 @@ def test_int_promote_fast_path_vs_oracle(shape):
     qa = quantize_triton(torch.randn(m, k, generator=g).cuda(), SCHEMES["int8_row"])
     qw = quantize_triton((torch.randn(n, k, generator=g) * 0.02).cuda(), SCHEMES["int4_g128_zp"])
     z = qw.zero_point.repeat_interleave(128, dim=1)[:, :k]
-    a = as_operand(qa, compact=compact)
+    a = as_operand(qa)
     b = Operand(qw.values.float() - z, IntFormat("int5", 5), qw.scale, FP16, "k", 128)
     spec = MMASpec("cofda", f_bits=23, chunk_size=32, promote_interval=128, out_format="fp32")
     got = gemm_triton(a, b, spec).cpu().numpy()
@@ -388,7 +388,7 @@ def test_int_tensor_core_path(shape):
     qa = quantize_triton(x.cuda(), SCHEMES["int8_row"])
     qw = quantize_triton(w.cuda(), SCHEMES["int4_g128_zp"])
     z = qw.zero_point.repeat_interleave(128, dim=1)[:, :k]
-    a = as_operand(qa, compact=compact)
+    a = as_operand(qa)
     b = Operand(qw.values.float() - z, IntFormat("int5", 5), qw.scale, FP16, "k", 128)
     spec = MMASpec("cofda", f_bits=23, chunk_size=32, promote_interval=128, out_format="fp32")
     before = exact_fallbacks()
