@@ -167,8 +167,10 @@ int tc_gemm(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec, c
  * arguments and result as tc_gemm minus the workspace; the scratch comes from a fixed 32 MiB array
  * inside the library (held on every GPU that loads the library, until exit). Operands whose
  * tc_gemm_workspace() exceeds 32 MiB are rejected with TC_INVALID_ARGUMENT. The first call on a
- * device looks up that array's device address, so make it before any stream capture. All calls
- * share the array: calls whose GPU work can overlap race and must not be issued. Allocates nothing. */
+ * device looks up that array's device address, so make it before any stream capture. The array used is
+ * the current device's: call with the device of out (and of stream) current; an out on another
+ * device is rejected with TC_INVALID_ARGUMENT. All calls share the array: calls whose GPU work can
+ * overlap race and must not be issued. Allocates nothing. */
 int tc_gemm_noalloc(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec, const float *bias,
                     void *out, tc_stream stream);
 
@@ -191,6 +193,19 @@ uint64_t tc_launch_count(void);
  * has actually run (the fast kernel declined the operands or one of its waits ran out). Waits for the
  * device. */
 int tc_exact_fallbacks(uint64_t *count);
+
+/* Of those runs, how many followed a fast kernel whose bounded wait ran out (it set its status word,
+ * drained its own copies and MMAs, freed its TMEM and returned). Waits for the device. No counterpart
+ * in TriCast, whose Triton kernels have no bounded waits. */
+int tc_wait_timeouts(uint64_t *count);
+
+/* Poll limit of the pipeline waits (on shared-memory barriers) of the staged GEMM kernels launched
+ * from now on, process-wide; polls < 0 restores the defaults (about 2**16 suspended or 2**22 plain
+ * polls, seconds). With polls = 0 every such wait gives up at once: the kernel takes its timeout path
+ * and the exact kernel queued behind it recomputes the product, so results stay exact. The waits that
+ * drain a kernel's own copies and MMAs before it exits keep the default limit. No counterpart in
+ * TriCast: it exists to test the timeout path without hanging or faulting a GPU. */
+int tc_set_wait_limit(int32_t polls);
 
 /* Silicon probe, not part of the emulation API: out[M][N] = sum_k A[m][k] * B[n][k] computed by the
  * B200's own FP8 tensor-core MMA (tcgen05.mma kind::f8f6f4, fp32 accumulator, K issued 32 at a time

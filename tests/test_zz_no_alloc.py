@@ -16,8 +16,8 @@ import torch
 from tests.conftest import bits_equal
 from tricast_b200 import _native as N
 from tricast_b200 import as_operand, gemm_triton, quantize_triton
-from tricast_b200.mma import _Prepared, mma_spec_struct, resolve_scale_apply
-from tricast_b200.spec import PRESETS, SCHEMES
+from tricast_b200.mma import _Prepared, exact_fallbacks, mma_spec_struct, resolve_scale_apply
+from tricast_b200.spec import PRESETS, SCHEMES, MMASpec
 
 pytestmark = pytest.mark.gpu
 
@@ -34,11 +34,22 @@ def _noalloc(a, b, spec, bias=None):
     ms = mma_spec_struct(spec, resolve_scale_apply(spec, a, b))
     from tricast_b200.formats import container_dtype
 
-    out = torch.empty((a.rows, b.rows), device=a.values.device, dtype=container_dtype(spec.out_format))
-    bias_t = None if bias is None else bias.float().contiguous()
-    N.check(N.lib().tc_gemm_noalloc(pa.desc, pb.desc, ms, N.ptr(bias_t), N.ptr(out), N.stream_of(a.values.device)),
-            "tc_gemm_noalloc")
+    dev = a.values.device
+    with torch.cuda.device(dev):  # the fixed scratch array used is the current device's
+        out = torch.empty((a.rows, b.rows), device=dev, dtype=container_dtype(spec.out_format))
+        bias_t = None if bias is None else bias.float().contiguous()
+        N.check(N.lib().tc_gemm_noalloc(pa.desc, pb.desc, ms, N.ptr(bias_t), N.ptr(out), N.stream_of(dev)),
+                "tc_gemm_noalloc")
     return out
+
+
+def _launches(fn):
+    """(result, kernels the library launched for it, exact fallbacks it caused)."""
+    torch.cuda.synchronize()
+    l0, f0 = N.lib().tc_launch_count(), exact_fallbacks()
+    out = fn()
+    torch.cuda.synchronize()
+    return out, N.lib().tc_launch_count() - l0, exact_fallbacks() - f0
 
 
 def test_noalloc_equals_tc_gemm_on_consecutive_calls():
@@ -47,12 +58,25 @@ def test_noalloc_equals_tc_gemm_on_consecutive_calls():
              (_operand("mxfp4", 130, 1040, 3), _operand("mxfp4", 65, 1040, 4)),
              (_operand("nvfp4", 192, 1024, 1), _operand("nvfp4", 320, 1024, 2, 0.02))]
     for a, b in cases:
-        first = _noalloc(a, b, spec)
+        first, n_first, fb_first = _launches(lambda: _noalloc(a, b, spec))
         second = _noalloc(a, b, spec)  # the scratch now holds this call's own leftovers
-        want = gemm_triton(a, b, spec)
-        torch.cuda.synchronize()
+        want, n_want, _ = _launches(lambda: gemm_triton(a, b, spec))
         assert bits_equal(first.cpu().numpy(), want.cpu().numpy())
         assert bits_equal(second.cpu().numpy(), want.cpu().numpy())
+        # The same fast kernels ran on the fixed array (tc_gemm's launch count, no exact fallback).
+        assert fb_first == 0 and n_first == n_want
+
+
+def test_noalloc_fp64_and_fp32_fma_take_the_fast_kernel():
+    """fp64 / fp32_fma need no scratch at all; they still run tc_gemm's FMA-chain kernel, not the
+    generic exact one."""
+    a, b = _operand("nvfp4", 96, 512, 11), _operand("nvfp4", 80, 512, 12, 0.02)
+    for spec in (MMASpec("fp64", out_format="fp32"), MMASpec("fp32_fma", out_format="fp32")):
+        want, n_want, _ = _launches(lambda: gemm_triton(a, b, spec))
+        for _ in range(2):
+            got, n_got, fb = _launches(lambda: _noalloc(a, b, spec))
+            assert bits_equal(got.cpu().numpy(), want.cpu().numpy())
+            assert fb == 0 and n_got == n_want == 1
 
 
 def test_noalloc_without_fast_path_and_with_bias():

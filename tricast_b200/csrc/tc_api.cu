@@ -15,6 +15,23 @@ void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 void set_error(const std::string &msg) { g_last_error = msg; }
 
+static std::atomic<int> g_wait_polls{-1};
+int wait_polls() { return g_wait_polls.load(std::memory_order_relaxed); }
+
+int sm_count() {
+  static std::atomic<int> counts[128];
+  int dev = 0;
+  // A failed query leaves a grid of one block per 'SM' of a one-SM device: slower, never wrong (the
+  // kernels are grid-stride), and the launch reports the CUDA error anyway.
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 1;
+  int c = counts[dev].load(std::memory_order_relaxed);
+  if (c <= 0) {
+    if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0) return 1;
+    counts[dev].store(c, std::memory_order_relaxed);
+  }
+  return c;
+}
+
 static uint32_t host_f2u(float v) {
   uint32_t u;
   std::memcpy(&u, &v, 4);
@@ -125,5 +142,10 @@ Fmt derive(const tc_format &f) {
 extern "C" const char *tc_last_error(void) { return tc::g_last_error.c_str(); }
 
 extern "C" uint64_t tc_launch_count(void) { return tc::g_launches.load(std::memory_order_relaxed); }
+
+extern "C" int tc_set_wait_limit(int32_t polls) {
+  tc::g_wait_polls.store(polls < 0 ? -1 : polls, std::memory_order_relaxed);
+  return TC_OK;
+}
 
 extern "C" const char *tc_version(void) { return "tricast_b200 0.1.0 (sm_100a)"; }

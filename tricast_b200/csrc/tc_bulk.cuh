@@ -1,5 +1,9 @@
 // mbarrier and 1-D bulk-copy (TMA, no multicast) helpers shared by the staged kernels. Every wait
 // is bounded: mbar_wait gives up after about 2**22 polls and the caller reports the timeout.
+//
+// A kernel's pipeline waits take their poll limit from the launch (`polls`, negative = the default;
+// tc_set_wait_limit sets it process-wide so that a test can make a wait run out). The waits that drain
+// a kernel's own copies and MMAs before it exits always use the default limit.
 #pragma once
 
 #include <stdint.h>
@@ -31,17 +35,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after ~2**22 polls (each try_wait itself suspends for a while).
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-  for (int i = 0; i < (1 << 22); ++i)
+// Bounded wait: gives up after ~2**22 polls (each try_wait itself suspends for a while), or after
+// `polls` polls when that is not negative (0: gives up at once).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int polls = -1) {
+  const int limit = polls < 0 ? (1 << 22) : polls;
+  for (int i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
 
 // Bounded wait that lets the hardware suspend the thread between polls (up to ~64 us each), so
-// waiting warps do not take issue slots from working ones; gives up after ~2**16 polls (seconds).
-__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity) {
-  for (int i = 0; i < (1 << 16); ++i) {
+// waiting warps do not take issue slots from working ones; gives up after ~2**16 polls (seconds), or
+// after `polls` polls when that is not negative.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, int polls = -1) {
+  const int limit = polls < 0 ? (1 << 16) : polls;
+  for (int i = 0; i < limit; ++i) {
     uint32_t ok;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"

@@ -40,6 +40,12 @@ double fmt_min_scale(const tc_format &f);   // min_subnormal (floats) / min_norm
 int fmt_emax_elem(const tc_format &f);      // floor(log2(max_normal))
 void set_error(const std::string &msg);
 void count_launch();  // every kernel launch of the library; read by tc_launch_count()
+// Multiprocessor count of the current device (queried once per device ordinal); grid-stride
+// kernels cap their grids at a multiple of it.
+int sm_count();
+// Poll limit of the staged kernels' pipeline waits for the next launches (negative = the kernels'
+// defaults); set by tc_set_wait_limit, read at every launch.
+int wait_polls();
 
 // ---------------------------------------------------------------- small device helpers
 __host__ __device__ __forceinline__ uint32_t f2u(float v) {

@@ -240,6 +240,7 @@ struct GemmArgs {
   void *out;
   const int32_t *flag;   // nonzero: the fast path is not valid for these operands
   int32_t *status;       // set to 1 when a bounded wait gives up
+  int wait_polls;        // poll limit of the pipeline waits (negative: default)
 };
 
 }  // namespace fp4

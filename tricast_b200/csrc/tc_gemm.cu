@@ -16,10 +16,15 @@ namespace tc {
 // the common case (flag clear) costs a few hundred blocks that read two words and exit.
 // Runs of the exact kernel behind a fast kernel that declined its operands (or timed out), per device.
 __device__ unsigned long long g_exact_fallbacks;
+// Of those, the runs whose fast kernel reported a bounded wait that ran out (its status word).
+__device__ unsigned long long g_wait_timeouts;
 
 __global__ void __launch_bounds__(256) gemm_generic_kernel(GemmDesc g, const int32_t *only_if_flag) {
   if (only_if_flag && only_if_flag[0] == 0 && only_if_flag[1] == 0) return;  // the fast kernel took it
-  if (only_if_flag && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(&g_exact_fallbacks, 1ull);
+  if (only_if_flag && blockIdx.x == 0 && threadIdx.x == 0) {
+    atomicAdd(&g_exact_fallbacks, 1ull);
+    if (only_if_flag[1]) atomicAdd(&g_wait_timeouts, 1ull);
+  }
   const int64_t tiles_n = (g.N + 15) / 16, tiles = tiles_n * ((g.M + 15) / 16);
   for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
     const int64_t n = (tile % tiles_n) * 16 + (threadIdx.x & 15);
@@ -127,10 +132,7 @@ int build_desc(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec
 
 void launch_generic(const GemmDesc &g, const int32_t *only_if_flag, cudaStream_t s) {
   const int64_t tiles = ((g.N + 15) / 16) * ((g.M + 15) / 16);
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t cap = (int64_t)sms * 8;
+  const int64_t cap = (int64_t)sm_count() * 8;
   gemm_generic_kernel<<<(unsigned)(tiles < cap ? tiles : cap), 256, 0, s>>>(g, only_if_flag);
   count_launch();
 }
@@ -174,11 +176,20 @@ extern "C" int tc_exact_fallbacks(uint64_t *count) {
   return TC_OK;
 }
 
+extern "C" int tc_wait_timeouts(uint64_t *count) {
+  if (!count) return set_error("tc_wait_timeouts: null argument"), TC_INVALID_ARGUMENT;
+  unsigned long long v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v));
+  if (e != cudaSuccess) return set_error(std::string("tc_wait_timeouts: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
+  *count = (uint64_t)v;
+  return TC_OK;
+}
+
 extern "C" int tc_any_nonfinite(const void *values, int32_t dtype, int64_t n, int32_t *flag, tc_stream stream) {
   if (n <= 0) return TC_OK;
   if (!values || !flag || dtype < 0 || dtype > 2) return set_error("tc_any_nonfinite: bad argument"), TC_INVALID_ARGUMENT;
   int64_t blocks = (n + 255) / 256;
-  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (blocks > (int64_t)sm_count() * 8) blocks = (int64_t)sm_count() * 8;
   any_nonfinite_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(values, dtype, n, flag);
   ::tc::count_launch();
   cudaError_t e = cudaGetLastError();

@@ -125,6 +125,7 @@ struct Args {
   GemmDesc g;                    // epilogue (scales, alpha, bias, output)
   const int32_t *flag;
   int32_t *status;
+  int wait_polls;  // poll limit of the pipeline waits (negative: default)
 };
 
 template <int CS, class T>
@@ -177,9 +178,13 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
   bool timed_out = false;
   for (int64_t ch = 0; ch < p.nchunks; ++ch) {
     const int s = (int)(ch % kStages);
-    if (!mbar_wait(&full[s], (uint32_t)((ch / kStages) & 1))) timed_out = true;
+    if (!mbar_wait(&full[s], (uint32_t)((ch / kStages) & 1), p.wait_polls)) timed_out = true;
     if (__syncthreads_or(timed_out)) {
-      if (threadIdx.x == 0) atomicExch(p.status, 1);
+      if (threadIdx.x == 0) {
+        atomicExch(p.status, 1);
+        // Chunks ch .. ch + kStages - 1 may still be in flight: they land before the CTA exits.
+        for (int64_t u = ch; u < ch + kStages && u < p.nchunks; ++u) mbar_wait(&full[u % kStages], (uint32_t)((u / kStages) & 1));
+      }
       return;
     }
     const Stage<CS, T> &st = stages[s];
@@ -423,7 +428,7 @@ int launch_cofda(const GemmDesc &g, void *workspace, size_t workspace_bytes, cud
     e.flag = flag;
     int64_t work = (e.rows_pad / 2) * p.nchunks * p.CS;
     int64_t blocks = (work + 255) / 256;
-    if (blocks > 148 * 16) blocks = 148 * 16;
+    if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
     if (p.wide) cofda::encode_kernel<double><<<(unsigned)blocks, 256, 0, s>>>(e);
     else cofda::encode_kernel<float><<<(unsigned)blocks, 256, 0, s>>>(e);
     count_launch();
@@ -449,6 +454,7 @@ int launch_cofda(const GemmDesc &g, void *workspace, size_t workspace_bytes, cud
   a.g = g;
   a.flag = flag;
   a.status = flag + 1;
+  a.wait_polls = wait_polls();
   int st;
   if (p.CS == 32) st = g.rne ? launch_cofda_kernel<32, true>(a, p.wide, s) : launch_cofda_kernel<32, false>(a, p.wide, s);
   else if (p.CS == 16) st = g.rne ? launch_cofda_kernel<16, true>(a, p.wide, s) : launch_cofda_kernel<16, false>(a, p.wide, s);

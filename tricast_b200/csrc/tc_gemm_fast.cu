@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(256, 2) gdfs_fp4_kernel(GemmArgs g) {
   int64_t t = 0;
   for (; t < g.ntiles; ++t) {
     const int s = (int)(t % kStages);
-    const bool landed = mbar_wait(&full[s], (uint32_t)((t / kStages) & 1));
+    const bool landed = mbar_wait(&full[s], (uint32_t)((t / kStages) & 1), g.wait_polls);
     if (__any_sync(0xFFFFFFFFu, !landed)) {
       if ((threadIdx.x & 31) == 0) atomicExch(g.status, 1);
       break;
@@ -388,7 +388,7 @@ __global__ void __launch_bounds__(256, 2) gdfs_fp4_kernel(GemmArgs g) {
     if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[s]);
     if (threadIdx.x == 0 && producer_ok && t >= 1 && t - 1 + kStages < g.ntiles) {
       const int sp = (int)((t - 1) % kStages);
-      if (mbar_wait(&empty[sp], (uint32_t)(((t - 1) / kStages) & 1))) {
+      if (mbar_wait(&empty[sp], (uint32_t)(((t - 1) / kStages) & 1), g.wait_polls)) {
         issue(t - 1 + kStages, sp);
       } else {
         atomicExch(g.status, 1);
@@ -541,11 +541,11 @@ int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
     e.vec = ((uintptr_t)o.v % 16 == 0) && ((o.K * esz) % 16 == 0);
     int64_t work = p.ntiles * p.ng * e.rows_pad;
     int64_t blocks = (work + 255) / 256;
-    if (blocks > 148 * 16) blocks = 148 * 16;
+    if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
     fp4::encode_fp4_kernel<<<(unsigned)blocks, 256, 0, s>>>(e);
     count_launch();
     const int64_t twork = p.ntiles * e.rows_pad;
-    const int64_t tblocks = std::min<int64_t>((twork + 255) / 256, 148 * 16);
+    const int64_t tblocks = std::min<int64_t>((twork + 255) / 256, (int64_t)sm_count() * 16);
     fp4::tile_words_kernel<<<(unsigned)tblocks, 256, 0, s>>>(e.s, e.rows_pad, p.ntiles, p.ng,
                                                              reinterpret_cast<int32_t *>(ws + p.off[side * 5 + 3]),
                                                              reinterpret_cast<int2 *>(ws + p.off[side * 5 + 4]));
@@ -582,6 +582,7 @@ int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
   a.out = g.out;
   a.flag = flag;
   a.status = flag + 1;
+  a.wait_polls = wait_polls();
   int st = launch_fp4_gemm_tc(a, p.ng, s);  // tensor cores for NG <= 4
   if (st == TC_UNSUPPORTED) switch (p.ng) {
     case 1: st = launch_fp4_gemm<1>(a, g.M, g.N, s); break;

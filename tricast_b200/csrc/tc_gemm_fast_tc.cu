@@ -152,8 +152,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdfs_fp4_tc_kernel(const __grid_c
       for (int64_t t = 0; t < kStages && t < g.ntiles; ++t) issue(t);
       for (int64_t t = 0; t < g.ntiles; ++t) {
         const int s = (int)(t % kStages), b = (int)(t & 1);
-        if (t >= 2 && !mbar_wait_sleep(&tempty[b], (uint32_t)(((t - 2) >> 1) & 1))) { ok = false; break; }
-        if (!mbar_wait_sleep(&full[s], (uint32_t)((t / kStages) & 1))) { ok = false; break; }
+        if (t >= 2 && !mbar_wait_sleep(&tempty[b], (uint32_t)(((t - 2) >> 1) & 1), g.wait_polls)) { ok = false; break; }
+        if (!mbar_wait_sleep(&full[s], (uint32_t)((t / kStages) & 1), g.wait_polls)) { ok = false; break; }
         waited_full = t + 1;
         tc5::fence_after_sync();
         const Stage<NG> &st = stages[s];
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdfs_fp4_tc_kernel(const __grid_c
         // Refill the stage of tile t - 1 (released by its MMAs and the epilogue) with tile t - 1 + kStages.
         const int64_t prev = t - 1;
         if (prev >= 0 && prev + kStages < g.ntiles) {
-          if (!mbar_wait_sleep(&empty[prev % kStages], (uint32_t)((prev / kStages) & 1))) { ok = false; break; }
+          if (!mbar_wait_sleep(&empty[prev % kStages], (uint32_t)((prev / kStages) & 1), g.wait_polls)) { ok = false; break; }
           issue(prev + kStages);
         }
       }
@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdfs_fp4_tc_kernel(const __grid_c
     bool ok = true;
     for (int64_t t = 0; t < g.ntiles; ++t) {
       const int s = (int)(t % kStages), b = (int)(t & 1);
-      ok = mbar_wait_sleep(&tfull[b], (uint32_t)((t >> 1) & 1));
+      ok = mbar_wait_sleep(&tfull[b], (uint32_t)((t >> 1) & 1), g.wait_polls);
       if (!__all_sync(0xFFFFFFFFu, ok)) {
         if (lane == 0) atomicExch(g.status, 1);
         ok = false;

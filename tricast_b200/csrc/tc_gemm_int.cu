@@ -79,6 +79,7 @@ struct Args {
   GemmDesc g;
   const int32_t *flag;
   int32_t *status;
+  int wait_polls;  // poll limit of the pipeline waits (negative: default)
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -97,8 +98,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-  for (int i = 0; i < (1 << 22); ++i)
+// Bounded wait: ~2**22 polls, or `polls` when that is not negative (0: gives up at once).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int polls = -1) {
+  const int limit = polls < 0 ? (1 << 22) : polls;
+  for (int i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
@@ -151,9 +154,13 @@ __global__ void __launch_bounds__(256) int_kernel(Args p) {
   bool timed_out = false;
   for (int64_t sp = 0; sp < p.nspans; ++sp) {
     const int s = (int)(sp % kStages);
-    if (!mbar_wait(&full[s], (uint32_t)((sp / kStages) & 1))) timed_out = true;
+    if (!mbar_wait(&full[s], (uint32_t)((sp / kStages) & 1), p.wait_polls)) timed_out = true;
     if (__syncthreads_or(timed_out)) {
-      if (threadIdx.x == 0) atomicExch(p.status, 1);
+      if (threadIdx.x == 0) {
+        atomicExch(p.status, 1);
+        // Spans sp .. sp + kStages - 1 may still be in flight: they land before the CTA exits.
+        for (int64_t u = sp; u < sp + kStages && u < p.nspans; ++u) mbar_wait(&full[u % kStages], (uint32_t)((u / kStages) & 1));
+      }
       return;
     }
     const Stage &st = stages[s];
@@ -303,7 +310,7 @@ int launch_int(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaS
     e.flag = flag;
     int64_t work = e.rows_pad * p.nspans * (intk::kSpan / 4);
     int64_t blocks = (work + 255) / 256;
-    if (blocks > 148 * 16) blocks = 148 * 16;
+    if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
     intk::encode_kernel<<<(unsigned)blocks, 256, 0, s>>>(e);
     count_launch();
   }
@@ -323,6 +330,7 @@ int launch_int(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaS
   a.g = g;
   a.flag = flag;
   a.status = flag + 1;
+  a.wait_polls = wait_polls();
   size_t smem = sizeof(intk::Stage) * intk::kStages;
   auto kern = p.promote ? intk::int_kernel<true> : intk::int_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

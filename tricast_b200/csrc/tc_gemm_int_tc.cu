@@ -102,6 +102,7 @@ struct Args {
   GemmDesc g;
   const int32_t *flag;
   int32_t *status;
+  int wait_polls;  // poll limit of the pipeline waits (negative: default)
 };
 
 // Instruction descriptor: kind::i8, D int32, A and B signed int8, both K-major, M = 128, N = 128.
@@ -150,8 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1) int_tc_kernel(Args p) {
         const int s = (int)(sp % kStages);
         const int b = PROMOTE ? (int)(sp & 1) : 0;
         // The accumulator buffer is free once the epilogue has read span sp - 2 from it.
-        if (PROMOTE && sp >= 2 && !mbar_wait_sleep(&tempty[b], (uint32_t)(((sp - 2) >> 1) & 1))) { ok = false; break; }
-        if (!mbar_wait_sleep(&full[s], (uint32_t)((sp / kStages) & 1))) { ok = false; break; }
+        if (PROMOTE && sp >= 2 && !mbar_wait_sleep(&tempty[b], (uint32_t)(((sp - 2) >> 1) & 1), p.wait_polls)) { ok = false; break; }
+        if (!mbar_wait_sleep(&full[s], (uint32_t)((sp / kStages) & 1), p.wait_polls)) { ok = false; break; }
         waited_full = sp + 1;
         tc5::fence_after_sync();
         const unsigned char *sa = smem_raw + (size_t)s * 2 * kSpanBytes, *sb = sa + kSpanBytes;
@@ -168,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1) int_tc_kernel(Args p) {
         // kStages after it, so the tensor pipe always has the next span's MMAs queued.
         const int64_t prev = sp - 1;
         if (prev >= 0 && prev + kStages < p.nspans) {
-          if (!mbar_wait_sleep(&empty[prev % kStages], (uint32_t)((prev / kStages) & 1))) { ok = false; break; }
+          if (!mbar_wait_sleep(&empty[prev % kStages], (uint32_t)((prev / kStages) & 1), p.wait_polls)) { ok = false; break; }
           issue(prev + kStages);
         }
       }
@@ -192,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1) int_tc_kernel(Args p) {
     const int64_t rounds = PROMOTE ? p.nspans : 1;
     for (int64_t sp = 0; sp < rounds; ++sp) {
       const int b = PROMOTE ? (int)(sp & 1) : 0;
-      ok = mbar_wait_sleep(&tfull[b], PROMOTE ? (uint32_t)((sp >> 1) & 1) : 0u);
+      ok = mbar_wait_sleep(&tfull[b], PROMOTE ? (uint32_t)((sp >> 1) & 1) : 0u, p.wait_polls);
       if (!__all_sync(0xFFFFFFFFu, ok)) {
         if (lane == 0) atomicExch(p.status, 1);
         ok = false;
@@ -289,13 +290,13 @@ int launch_int_tc(const GemmDesc &g, bool promote, void *workspace, size_t works
     e.out = reinterpret_cast<uint4 *>(ws + (side ? p.off_b : p.off_a));
     e.flag = flag;
     const int64_t work = e.rows_pad * p.nspans * (itc::kSpan / 16);
-    const int64_t blocks = std::min<int64_t>((work + 255) / 256, 148 * 16);
+    const int64_t blocks = std::min<int64_t>((work + 255) / 256, (int64_t)sm_count() * 16);
     itc::encode_kernel<<<(unsigned)blocks, 256, 0, s>>>(e);
     count_launch();
     if (promote && o.skind == SK_K) {
       const int64_t n = e.rows_pad * p.nspans;
       float *dst = reinterpret_cast<float *>(ws + (side ? p.off_sb : p.off_sa));
-      itc::span_scales_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 148 * 8), 256, 0, s>>>(
+      itc::span_scales_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8), 256, 0, s>>>(
           o.scale, o.nkd, o.kd, o.rows, e.rows_pad, p.nspans, dst);
       count_launch();
     }
@@ -316,6 +317,7 @@ int launch_int_tc(const GemmDesc &g, bool promote, void *workspace, size_t works
   a.g = g;
   a.flag = flag;
   a.status = flag + 1;
+  a.wait_polls = wait_polls();
   const size_t smem = (size_t)itc::kStages * 2 * itc::kSpanBytes;
   auto kern = promote ? itc::int_tc_kernel<true> : itc::int_tc_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -467,7 +467,7 @@ int launch_fp4_gemv(const GemmDesc &g, int ng, void *workspace, size_t workspace
     const int esz = g.a.dt == TC_F32 ? 4 : 2;
     e.vec = ((uintptr_t)g.a.v % 16 == 0) && ((g.a.K * esz) % 16 == 0);
     const int64_t work = p.ngroups_pad * p.mp;
-    const int64_t blocks = std::min<int64_t>((work + 255) / 256, 148 * 16);
+    const int64_t blocks = std::min<int64_t>((work + 255) / 256, (int64_t)sm_count() * 16);
     fp4::encode_fp4_kernel<<<(unsigned)blocks, 256, 0, s>>>(e);
     count_launch();
   }

@@ -420,7 +420,7 @@ static int launch_cofda_gemv_typed(const GemmDesc &g, const CofdaGemvPlan &p, ch
     e.exp = reinterpret_cast<int16_t *>(ws + p.off_exp);
     e.flag = flag;
     const int64_t work = g.M * p.Kp;
-    const int64_t blocks = std::min<int64_t>((work + 255) / 256, 148 * 8);
+    const int64_t blocks = std::min<int64_t>((work + 255) / 256, (int64_t)sm_count() * 8);
     cgemv::prep_a_kernel<T><<<(unsigned)blocks, 256, 0, s>>>(e);
     count_launch();
   }

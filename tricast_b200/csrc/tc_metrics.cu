@@ -69,7 +69,7 @@ extern "C" int tc_error_stats(const void *ref, int32_t ref_dtype, const void *em
     return TC_INVALID_ARGUMENT;
   }
   int64_t blocks = (n + 255) / 256;
-  if (blocks > 148 * 4) blocks = 148 * 4;
+  if (blocks > (int64_t)tc::sm_count() * 4) blocks = (int64_t)tc::sm_count() * 4;
   tc::error_stats_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(ref, ref_dtype, emu, emu_dtype, n, sums);
   ::tc::count_launch();
   cudaError_t e = cudaGetLastError();

@@ -17,6 +17,10 @@
 // path's status words are cleared on the stream at the start of each call, and everything else is
 // fully rewritten before it is read. Calls whose GPU work overlaps (different streams, or other host
 // threads, without ordering between them) race on the array and must not be issued.
+//
+// The array used is the current device's, so the output (and the stream) must belong to the device
+// that is current on the calling thread; a call whose output lives on another device is rejected
+// with TC_INVALID_ARGUMENT before anything is launched.
 #include <mutex>
 #include <string>
 
@@ -49,6 +53,25 @@ static int scratch_on_current_device(void **out) {
   return TC_OK;
 }
 
+// The output must be memory of the current device (the scratch array resolved above is that
+// device's): a device pointer of another device is refused.
+static int out_on_current_device(const void *out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(std::string("tc_gemm_noalloc: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
+  cudaPointerAttributes attr;
+  e = cudaPointerGetAttributes(&attr, out);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // clear the sticky-free error of a pointer CUDA does not know
+    return set_error("tc_gemm_noalloc: the output is not CUDA memory"), TC_INVALID_ARGUMENT;
+  }
+  if (attr.type == cudaMemoryTypeDevice && attr.device != dev)
+    return set_error("tc_gemm_noalloc: the output lives on device " + std::to_string(attr.device) +
+                     " but device " + std::to_string(dev) + " is current; make the output's device current"),
+           TC_INVALID_ARGUMENT;
+  return TC_OK;
+}
+
 }  // namespace tc
 
 using namespace tc;
@@ -66,12 +89,13 @@ extern "C" int tc_gemm_noalloc(const tc_operand *a, const tc_operand *b, const t
                      "-byte array; call tc_gemm with a workspace instead"),
            TC_INVALID_ARGUMENT;
   cudaStream_t s = (cudaStream_t)stream;
-  if (need > 0) {
-    void *scratch = nullptr;
-    if ((st = scratch_on_current_device(&scratch))) return st;
-    st = launch_fast(g, scratch, kScratchBytes, s);
-    if (st != TC_UNSUPPORTED) return st;
-  }
+  if ((st = out_on_current_device(out))) return st;
+  // Kernels that need no scratch (fp64 / fp32_fma chains) take the fast path with no workspace, as
+  // tc_gemm does; the others get the fixed array.
+  void *scratch = nullptr;
+  if (need > 0 && (st = scratch_on_current_device(&scratch))) return st;
+  st = launch_fast(g, scratch, need > 0 ? kScratchBytes : 0, s);
+  if (st != TC_UNSUPPORTED) return st;
   if ((g.M + 15) / 16 > 65535) return set_error("tc_gemm_noalloc: too many rows for the generic kernel"), TC_INVALID_ARGUMENT;
   launch_generic(g, nullptr, s);
   cudaError_t e = cudaGetLastError();

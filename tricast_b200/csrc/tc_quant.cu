@@ -75,17 +75,6 @@ __global__ void __launch_bounds__(256) cast_lean_kernel(const float *__restrict_
   for (int64_t i = (n8 << 3) + tid; i < n; i += stride) y[i] = lean_cast<RND>(x[i], l);
 }
 
-static int sm_count() {
-  static int count = 0;
-  if (!count) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
-    if (count <= 0) count = 148;
-  }
-  return count;
-}
-
 static int grid_for(int64_t work, int threads, int per_sm = 8) {
   int64_t blocks = (work + threads - 1) / threads;
   int64_t cap = (int64_t)sm_count() * per_sm;
