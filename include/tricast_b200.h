@@ -146,11 +146,21 @@ int tc_cast(const float *x, float *y, const uint32_t *noise, int64_t n, const tc
 size_t tc_quantize_workspace(int64_t rows, int64_t K, const tc_quant_spec *spec);
 
 /* Quantize x [rows, K] (x_dtype: TC_F32 / TC_BF16 / TC_F16) under spec, writing out. amax: NULL,
- * or a device fp32 scalar overriding the tensor amax (tensor granularity only). noise: NULL or
- * rows*K uint32; scale_noise: NULL or one uint32 per scale. */
+ * or a device fp32 scalar: for tensor granularity it overrides the tensor amax (TriCast's
+ * quantize(amax=...)); for a two-level spec of finer granularity (NVFP4) it is the tensor amax the
+ * global scale d2 is derived from, so that a shard of a larger tensor quantizes exactly as the same
+ * rows of the whole tensor would (an extension: TriCast accepts amax for tensor granularity only);
+ * other specs reject it. noise: NULL or rows*K uint32; scale_noise: NULL or one uint32 per scale. */
 int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t K, const tc_quant_spec *spec,
                 const float *amax, const uint32_t *noise, const uint32_t *scale_noise,
                 const tc_quant_out *out, void *workspace, size_t workspace_bytes, tc_stream stream);
+
+/* The amax of x (n elements of x_dtype) as the bits of the fp32 |x| maximum, NaN-propagating (NaN
+ * bits sort above Inf's), max-reduced into *bits (device uint32, cleared by the caller). A rank
+ * holding a row shard of a tensor reduces its shard's bits with the other ranks' (integer max) and
+ * passes the result, viewed as fp32, as tc_quantize's amax of a two-level spec. No counterpart in
+ * TriCast, whose tensors are never sharded. */
+int tc_tensor_amax_bits(const void *x, int32_t x_dtype, int64_t n, uint32_t *bits, tc_stream stream);
 
 /* Bytes of scratch tc_gemm needs for these operands and spec. */
 size_t tc_gemm_workspace(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec);
@@ -198,6 +208,11 @@ int tc_exact_fallbacks(uint64_t *count);
  * drained its own copies and MMAs, freed its TMEM and returned). Waits for the device. No counterpart
  * in TriCast, whose Triton kernels have no bounded waits. */
 int tc_wait_timeouts(uint64_t *count);
+
+/* How many (output, K tile) steps of the tensor-core GDFS-FP4 kernel, on the current device, failed
+ * the single-pass bounds and ran the exact two-pass step instead (exact either way; this counts how
+ * often the slow step runs). Waits for the device. No counterpart in TriCast. */
+int tc_exact_tile_steps(uint64_t *count);
 
 /* Poll limit of the pipeline waits (on shared-memory barriers) of the staged GEMM kernels launched
  * from now on, process-wide; polls < 0 restores the defaults (about 2**16 suspended or 2**22 plain

@@ -11,8 +11,6 @@ and that the context stays usable afterwards.
 
 from __future__ import annotations
 
-import ctypes as C
-
 import numpy as np
 import pytest
 import torch
@@ -22,7 +20,7 @@ from tests.conftest import bits_equal, first_mismatch
 from tricast_b200 import _native as N
 from tricast_b200 import as_operand, gemm_triton, quantize_triton
 from tricast_b200.formats import FP16, IntFormat
-from tricast_b200.mma import exact_fallbacks
+from tricast_b200.mma import exact_fallbacks, wait_timeouts
 from tricast_b200.operand import Operand
 from tricast_b200.spec import PRESETS, SCHEMES, MMASpec
 
@@ -30,9 +28,7 @@ pytestmark = pytest.mark.gpu
 
 
 def _timeouts() -> int:
-    count = C.c_uint64(0)
-    N.check(N.lib().tc_wait_timeouts(C.byref(count)), "tc_wait_timeouts")
-    return int(count.value)
+    return wait_timeouts()
 
 
 @pytest.fixture

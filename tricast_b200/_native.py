@@ -78,6 +78,8 @@ EXPORTS = {
     "tc_launch_count": (C.c_uint64, []),
     "tc_exact_fallbacks": (C.c_int, [C.POINTER(C.c_uint64)]),
     "tc_wait_timeouts": (C.c_int, [C.POINTER(C.c_uint64)]),
+    "tc_tensor_amax_bits": (C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_void_p, C.c_void_p]),
+    "tc_exact_tile_steps": (C.c_int, [C.POINTER(C.c_uint64)]),
     "tc_set_wait_limit": (C.c_int, [C.c_int32]),
     "tc_probe_mma_fp8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int32, C.c_void_p,
                                    C.c_void_p, C.c_void_p]),

@@ -176,6 +176,18 @@ extern "C" int tc_exact_fallbacks(uint64_t *count) {
   return TC_OK;
 }
 
+namespace tc {
+int exact_tile_steps(unsigned long long *count);
+}
+
+extern "C" int tc_exact_tile_steps(uint64_t *count) {
+  if (!count) return set_error("tc_exact_tile_steps: null argument"), TC_INVALID_ARGUMENT;
+  unsigned long long v = 0;
+  int st = tc::exact_tile_steps(&v);
+  *count = (uint64_t)v;
+  return st;
+}
+
 extern "C" int tc_wait_timeouts(uint64_t *count) {
   if (!count) return set_error("tc_wait_timeouts: null argument"), TC_INVALID_ARGUMENT;
   unsigned long long v = 0;

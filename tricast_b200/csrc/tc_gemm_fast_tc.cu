@@ -30,6 +30,10 @@
 namespace tc {
 namespace fp4tc {
 
+// (output, K tile) pairs that failed the single-pass bounds and took the exact two-pass step, summed
+// over every launch on this device (one warp-aggregated atomic per round of the rare path).
+__device__ unsigned long long g_exact_tile_steps;
+
 constexpr int kM = 128;  // rows of A per CTA (TMEM lanes)
 constexpr int kN = 64;   // columns of B per CTA
 constexpr int kStages = 4;
@@ -243,6 +247,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdfs_fp4_tc_kernel(const __grid_c
       // (non-inlined) function so that its registers do not count against this loop's.
       while (__any_sync(0xFFFFFFFFu, unsafe != 0)) {
         const int j = unsafe ? __ffs(unsafe) - 1 : -1;
+        const unsigned pending = __ballot_sync(0xFFFFFFFFu, j >= 0);
+        if (lane == 0) atomicAdd(&g_exact_tile_steps, (unsigned long long)__popc(pending));
         float cj = 0.0f;
 #pragma unroll
         for (int jj = 0; jj < kCols; ++jj) cj = jj == j ? c[jj] : cj;
@@ -294,6 +300,12 @@ static int launch_tc(const fp4::GemmArgs &args, cudaStream_t s) {
   dim3 grid((unsigned)((args.N + fp4tc::kN - 1) / fp4tc::kN), (unsigned)((args.M + fp4tc::kM - 1) / fp4tc::kM));
   fp4tc::gdfs_fp4_tc_kernel<NG, RNE><<<grid, fp4tc::kThreads, smem, s>>>(args);
   count_launch();
+  return TC_OK;
+}
+
+int exact_tile_steps(unsigned long long *count) {
+  cudaError_t e = cudaMemcpyFromSymbol(count, fp4tc::g_exact_tile_steps, sizeof(*count));
+  if (e != cudaSuccess) return set_error(std::string("tc_exact_tile_steps: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
   return TC_OK;
 }
 

@@ -377,9 +377,10 @@ __device__ __forceinline__ void tstat_add(Stat &s, float v) {
 
 // AMAX_ONLY: only the NaN-propagating amax (two-level specs and absmax / pow2 tensor scales); the
 // full statistic adds the signed range for zero points.
+// With AMAX_ONLY and amax_bits given, the amax goes to *amax_bits instead of out->amax.
 template <bool AMAX_ONLY>
 __global__ void __launch_bounds__(256) tensor_stats_kernel(const void *__restrict__ x, int dt, int64_t n, int vec,
-                                                           Stat *__restrict__ out) {
+                                                           Stat *__restrict__ out, uint32_t *amax_bits = nullptr) {
   Stat s;
   stat_init(s);
   int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -415,7 +416,7 @@ __global__ void __launch_bounds__(256) tensor_stats_kernel(const void *__restric
   for (int64_t i = done + tid; i < n; i += stride) tstat_add<AMAX_ONLY>(s, load_as_float(x, dt, i));
   if (AMAX_ONLY) {
     for (int m = 16; m; m >>= 1) s.amax = max(s.amax, __shfl_xor_sync(0xFFFFFFFFu, s.amax, m));
-    if ((threadIdx.x & 31) == 0) atomicMax(&out->amax, s.amax);
+    if ((threadIdx.x & 31) == 0) atomicMax(amax_bits ? amax_bits : &out->amax, s.amax);
   } else {
     for (int m = 16; m; m >>= 1) stat_merge(s, stat_shfl(s, m));
     if ((threadIdx.x & 31) == 0) {
@@ -981,10 +982,16 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
   if (!x || !spec || !out) return set_error("tc_quantize: null argument"), TC_INVALID_ARGUMENT;
   if (!out->values && !out->codes && !out->dequant)
     return set_error("tc_quantize: no element output (values, codes or dequant)"), TC_INVALID_ARGUMENT;
-  // An amax override replaces the statistic, so MSE and percentile specs search nothing: TriCast uses
-  // the absmax scale of the override (src/tricast/reference/quantize.py:282-285).
+  // For tensor granularity an amax override replaces the statistic, so MSE and percentile specs
+  // search nothing: TriCast uses the absmax scale of the override (src/tricast/reference/quantize.py:
+  // 282-285). For a two-level spec of finer granularity it is the tensor amax that the global decode
+  // scale d2 is derived from (a tensor sharded across devices, whose amax the caller reduced); the
+  // per-domain scales still come from the data, MSE and percentile searches included.
+  const bool d2_amax = amax && spec->granularity != GRAN_TENSOR;
+  if (d2_amax && !(spec->has_scale && spec->two_level))
+    return set_error("amax override requires tensor granularity and a scalar"), TC_INVALID_ARGUMENT;
   tc_quant_spec eff = *spec;
-  if (amax && spec->has_scale && (spec->scale_method == M_MSE || spec->scale_method == M_PERCENTILE))
+  if (amax && !d2_amax && spec->has_scale && (spec->scale_method == M_MSE || spec->scale_method == M_PERCENTILE))
     eff.scale_method = M_ABSMAX;
   spec = &eff;
   Plan pl;
@@ -993,8 +1000,6 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
   QParams &p = pl.p;
   if (p.has_scale && (!out->scale || (p.zp && !out->zero_point) || (p.two_level && !out->global_scale)))
     return set_error("tc_quantize: missing scale / zero_point / global_scale output"), TC_INVALID_ARGUMENT;
-  if (amax && spec->granularity != GRAN_TENSOR)
-    return set_error("amax override requires tensor granularity and a scalar"), TC_INVALID_ARGUMENT;
   if (pl.total > workspace_bytes || !workspace)
     return set_error("tc_quantize: workspace too small"), TC_WORKSPACE_TOO_SMALL;
   cudaStream_t s = (cudaStream_t)stream;
@@ -1173,4 +1178,17 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
                                                            out->codes, out->dequant);
   ::tc::count_launch();
   return launch_status("tc_quantize elements");
+}
+
+// Tensor amax of a shard, as the bit pattern of the fp32 |x| maximum (NaN-propagating: NaN bits sort
+// above Inf's), max-reduced into *bits (accumulating: the caller clears it, and may reduce several
+// shards or ranks into it with an integer max).
+extern "C" int tc_tensor_amax_bits(const void *x, int32_t x_dtype, int64_t n, uint32_t *bits, tc_stream stream) {
+  if (n <= 0) return TC_OK;
+  if (!x || !bits || x_dtype < 0 || x_dtype > 2) return set_error("tc_tensor_amax_bits: bad argument"), TC_INVALID_ARGUMENT;
+  const int vec = ((uintptr_t)x % 16) == 0;
+  tensor_stats_kernel<true><<<grid_for((n + 7) / 8, 256, 8), 256, 0, (cudaStream_t)stream>>>(x, x_dtype, n, vec,
+                                                                                             nullptr, bits);
+  ::tc::count_launch();
+  return launch_status("tc_tensor_amax_bits");
 }

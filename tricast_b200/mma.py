@@ -175,6 +175,26 @@ def exact_fallbacks(device=None) -> int:
     return int(count.value)
 
 
+def _device_counter(name: str, device) -> int:
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    count = C.c_uint64(0)
+    with torch.cuda.device(device):
+        N.check(getattr(N.lib(), name)(C.byref(count)), name)
+    return int(count.value)
+
+
+def wait_timeouts(device=None) -> int:
+    """Of the exact-kernel runs counted by :func:`exact_fallbacks`, those that followed a fast kernel
+    whose bounded wait ran out. Synchronises the device."""
+    return _device_counter("tc_wait_timeouts", device)
+
+
+def exact_tile_steps(device=None) -> int:
+    """(output, K tile) steps of the tensor-core GDFS-FP4 kernel that failed the single-pass bounds and
+    took the exact two-pass step. Synchronises the device."""
+    return _device_counter("tc_exact_tile_steps", device)
+
+
 def gemm(a, b, spec, *, bias: torch.Tensor | None = None) -> torch.Tensor:
     """TriCast ``gemm`` on CUDA operands (``mma/api.py:63-109``): activations [..., K] × weights [N, K]."""
     from .operand import Operand, as_operand
@@ -192,4 +212,4 @@ def gemm(a, b, spec, *, bias: torch.Tensor | None = None) -> torch.Tensor:
     return out.reshape(*a_shape[:-1], b_op.rows)
 
 
-__all__ = ["gemm_triton", "gemm", "exact_fallbacks", "resolve_scale_apply", "check_headroom", "get_format"]
+__all__ = ["gemm_triton", "gemm", "exact_fallbacks", "wait_timeouts", "exact_tile_steps", "resolve_scale_apply", "check_headroom", "get_format"]

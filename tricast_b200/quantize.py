@@ -127,9 +127,12 @@ class QuantExtras:
 
 def quantize_into(x: torch.Tensor, spec, *, amax=None, noise=None, seed: int = 0, scale_noise=None,
                   want_codes: bool = False, want_scale_codes: bool = False, want_dequant: bool = False,
-                  want_values: bool = True):
+                  want_values: bool = True, tensor_amax=None):
     """Quantize and return ``(QTensor, QuantExtras)``; the extras are written in the same pass.
-    ``want_values=False`` skips the QTensor values (the QTensor then carries ``values=None``)."""
+    ``want_values=False`` skips the QTensor values (the QTensor then carries ``values=None``).
+    ``tensor_amax`` (two-level specs such as NVFP4 only, not part of TriCast's API): the amax of the
+    whole tensor of which ``x`` is a row shard, from which the global scale is derived, so that the
+    shard's QTensor equals those rows of the whole tensor's."""
     if x.ndim == 0 or x.numel() == 0:
         raise ValueError("quantization needs a nonempty tensor of shape [..., K]")
     _validate_scale_spec(spec, scale_noise)
@@ -146,6 +149,12 @@ def quantize_into(x: torch.Tensor, spec, *, amax=None, noise=None, seed: int = 0
         if spec.granularity != "tensor" or amax.numel() != 1:
             raise ValueError("amax override requires tensor granularity and a scalar")
         amax = amax.to(device=device, dtype=torch.float32).reshape(()).contiguous()
+    if tensor_amax is not None:
+        if amax is not None or spec.scale is None or not spec.scale.two_level or spec.granularity == "tensor":
+            raise ValueError("tensor_amax needs a two-level spec of group, row or block granularity")
+        if tensor_amax.numel() != 1:
+            raise ValueError("tensor_amax must be a scalar")
+        amax = tensor_amax.to(device=device, dtype=torch.float32).reshape(()).contiguous()
     if (N.rounding_code(spec.rounding) == 5 and noise is None and spec.scale is not None
             and spec.scale.method == "mse"):
         raise ValueError("MSE with stochastic rounding requires explicit noise")
