@@ -34,12 +34,17 @@ def column_slab(n: int, world: int, rank: int) -> tuple[int, int]:
 
 
 def needs_tensor_amax(spec) -> bool:
-    """Whether the scheme's scales depend on the amax of the whole tensor."""
+    """Whether the scheme's scales depend on the amax of the whole tensor (and on nothing else of it).
+    Raises for tensor-granularity schemes whose scale needs more of the whole tensor than its amax
+    (zero points, MSE or percentile searches): those do not shard by rows."""
     sf = spec.scale
     if sf is None:
         return False
-    return bool(sf.two_level) or (spec.granularity == "tensor" and spec.zero_point == "none"
-                                  and sf.method in ("absmax", "pow2_floor", "pow2_ceil", "pow2_rne"))
+    if spec.granularity == "tensor":
+        if spec.zero_point != "none" or sf.method in ("mse", "percentile"):
+            raise ValueError(f"a {sf.method} tensor scale with zero point {spec.zero_point!r} does not shard by rows")
+        return True
+    return bool(sf.two_level)
 
 
 def shard_amax(x: torch.Tensor, group=None) -> torch.Tensor:
@@ -54,9 +59,16 @@ def shard_amax(x: torch.Tensor, group=None) -> torch.Tensor:
     with torch.cuda.device(x.device):
         N.check(N.lib().tc_tensor_amax_bits(N.ptr(x2d), N.dtype_code(x2d.dtype), x2d.numel(), N.ptr(bits),
                                             N.stream_of(x.device)), "tc_tensor_amax_bits")
+    return reduce_amax_bits(bits, group).view(torch.float32)
+
+
+def reduce_amax_bits(bits: torch.Tensor, group=None) -> torch.Tensor:
+    """Max of every rank's int32 amax bits (in place; one all-reduce when the group has several ranks)."""
+    import torch.distributed as dist
+
     if dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(bits, op=dist.ReduceOp.MAX, group=group)
-    return bits.view(torch.float32)
+    return bits
 
 
 def quantize_shard(x: torch.Tensor, spec, group=None):
@@ -81,9 +93,10 @@ def gather_columns(slab: torch.Tensor, n: int, group=None) -> torch.Tensor:
     most = max(e - s for s, e in widths)
     padded = slab.new_zeros((most, slab.shape[0]))
     padded[: slab.shape[1]] = slab.T
-    parts = slab.new_empty((world, most, slab.shape[0]))
+    parts = slab.new_empty((world * most, slab.shape[0]))
     dist.all_gather_into_tensor(parts, padded, group=group)
+    parts = parts.view(world, most, slab.shape[0])
     return torch.cat([parts[r, : e - s] for r, (s, e) in enumerate(widths)]).T.contiguous()
 
 
-__all__ = ["column_slab", "needs_tensor_amax", "shard_amax", "quantize_shard", "gather_columns"]
+__all__ = ["column_slab", "needs_tensor_amax", "shard_amax", "reduce_amax_bits", "quantize_shard", "gather_columns"]

@@ -18,8 +18,11 @@ Recipe presets keep TriCast's default ``out_format=bf16``. Metrics are TriCast's
 (``analysis.py:29-62``): MSE, SQNR (dB), max abs error, relative Frobenius norm and cosine, from
 fp64 sums computed on the device.
 
-Layers are sharded across ranks by longest-processing-time on their MAC count; the only
-collective is an NCCL ``all_gather`` of the ``[layers, formats, 6]`` fp64 metric sums. With
+Layers are sharded across ranks by longest-processing-time on the measured device time of one layer
+of each shape (:func:`measure_costs`, which also warms every shape up at full size) or, without
+measurements, on their MAC count; the collectives are an NCCL ``all_gather`` of the
+``[layers, formats, 6]`` fp64 metric sums and two small ones for the cost table and the per-rank
+timing breakdown. With
 ``out_dir`` each finished layer writes a JSON record and a rerun skips recorded layers.
 """
 
@@ -97,15 +100,58 @@ def reference(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return gemm_triton(as_operand(x, compact=True), as_operand(w, compact=True), MMASpec("fp64", out_format="fp32"))
 
 
-def shard(layers: list, world: int, rank: int) -> list:
-    """Longest-processing-time assignment of layers to ranks by MAC count (deterministic)."""
-    loads = [0] * world
+def shard(layers: list, world: int, rank: int, cost: dict | None = None) -> list:
+    """Longest-processing-time assignment of layers to ranks (deterministic). A layer's cost is
+    ``cost[(in, out)]`` (e.g. measured seconds per layer of that shape) or, without a table, its MAC
+    count."""
+    def weight(e):
+        return cost[(e[2], e[3])] if cost else e[2] * e[3]
+
+    loads = [0.0] * world
     owner = {}
-    for entry in sorted(layers, key=lambda e: (-(e[2] * e[3]), e[0])):
+    for entry in sorted(layers, key=lambda e: (-weight(e), e[0])):
         r = min(range(world), key=lambda i: (loads[i], i))
         owner[entry[0]] = r
-        loads[r] += entry[2] * entry[3]
+        loads[r] += weight(entry)
     return [e for e in layers if owner[e[0]] == rank]
+
+
+def shapes(layers: list) -> list[tuple[int, int, int]]:
+    """(first layer index, in, out) of each distinct Linear shape, in layer order."""
+    seen = {}
+    for index, _, fin, fout in layers:
+        seen.setdefault((fin, fout), index)
+    return [(index, fin, fout) for (fin, fout), index in seen.items()]
+
+
+def measure_costs(cfg: SweepConfig, device, repeats: int = 2) -> dict:
+    """Device seconds of one layer's full work (make the tensors, fp64 reference, four emulated formats
+    and their error sums) for each distinct shape, at the configuration's token count. The first pass
+    of each shape is a warm-up (allocations, first launches); the cost is the minimum of ``repeats``
+    timed passes. With several ranks the table is averaged over them (one all-reduce), so that every
+    rank derives the same LPT assignment from it."""
+    import torch.distributed as dist
+
+    table = {}
+    for index, fin, fout in shapes(cfg.layers()):
+        entry = [(index, "", fin, fout)]
+        run_layers(entry, cfg, device)
+        best = float("inf")
+        for _ in range(repeats):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            run_layers(entry, cfg, device)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1) / 1e3)
+        table[(fin, fout)] = best
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        keys = sorted(table)
+        t = torch.tensor([table[k] for k in keys], dtype=torch.float64, device=device)
+        dist.all_reduce(t)
+        t /= dist.get_world_size()
+        table = dict(zip(keys, t.tolist()))
+    return table
 
 
 def run_layers(entries: list, cfg: SweepConfig, device, out_dir: str | None = None) -> torch.Tensor:
@@ -172,9 +218,13 @@ def results(table: torch.Tensor, cfg: SweepConfig) -> list[dict]:
     return out
 
 
-def run_sweep(cfg: SweepConfig | None = None, *, out_dir: str | None = None) -> tuple[list[dict] | None, float]:
+def run_sweep(cfg: SweepConfig | None = None, *, out_dir: str | None = None, costs: dict | None = None,
+              breakdown: dict | None = None) -> tuple[list[dict] | None, float]:
     """Run the sweep on this process's rank (torch.distributed initialised for world > 1).
-    Returns (records on rank 0 else None, seconds = max over ranks of device-timed wall time)."""
+    Returns (records on rank 0 else None, seconds = max over ranks of the device-timed span from the
+    first layer's first kernel to the last one's end). ``costs``: per-shape layer costs for the LPT
+    assignment (see :func:`measure_costs`; MAC counts without). ``breakdown``, when given, receives per
+    rank: layers, assigned cost, device seconds and host seconds spent enqueueing the work."""
     import torch.distributed as dist
 
     cfg = cfg or SweepConfig()
@@ -182,7 +232,7 @@ def run_sweep(cfg: SweepConfig | None = None, *, out_dir: str | None = None) -> 
     rank = dist.get_rank() if dist.is_initialized() else 0
     device = torch.device("cuda", torch.cuda.current_device())
     layers = cfg.layers()
-    mine = shard(layers, world, rank)
+    mine = shard(layers, world, rank, costs)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
@@ -192,13 +242,21 @@ def run_sweep(cfg: SweepConfig | None = None, *, out_dir: str | None = None) -> 
     start.record()
     sums = run_layers(mine, cfg, device, out_dir)
     end.record()
+    host = time.perf_counter() - t0
     end.synchronize()
     secs = max(start.elapsed_time(end) / 1e3, 0.0)
-    wall = torch.tensor([secs, time.perf_counter() - t0], dtype=torch.float64, device=device)
+    assigned = sum(costs[(e[2], e[3])] for e in mine) if costs else float(sum(e[2] * e[3] for e in mine))
+    mine_stats = torch.tensor([len(mine), assigned, secs, host], dtype=torch.float64, device=device)
+    every = [mine_stats]
     if world > 1:
-        dist.all_reduce(wall, op=dist.ReduceOp.MAX)
+        every = [torch.empty_like(mine_stats) for _ in range(world)]
+        dist.all_gather(every, mine_stats)
+    every = torch.stack(every).tolist()
+    if breakdown is not None:
+        breakdown.update({"layers": [int(r[0]) for r in every], "assigned_cost": [r[1] for r in every],
+                          "device_s": [r[2] for r in every], "host_enqueue_s": [r[3] for r in every]})
     table = gather(mine, sums, len(layers), world)
-    return (results(table, cfg) if rank == 0 else None), float(wall[0].item())
+    return (results(table, cfg) if rank == 0 else None), max(r[2] for r in every)
 
 
 def main() -> None:
@@ -219,7 +277,9 @@ def main() -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
-    records, secs = run_sweep(SweepConfig(args.blocks, args.tokens), out_dir=args.out)
+    cfg = SweepConfig(args.blocks, args.tokens)
+    costs = measure_costs(cfg, torch.device("cuda", local))
+    records, secs = run_sweep(cfg, out_dir=args.out, costs=costs)
     if records is not None:
         summary = {"layers": len(records), "formats": list(FORMATS), "seconds": secs, "n_gpus": world}
         if args.json:
