@@ -1,17 +1,21 @@
 """Benchmark of the TriCast emulation hot path on B200.
 
-Workload (the config the GEMM metric is quoted on): NVFP4 W4A4
-emulated GEMM. A = 2048x4096 bf16 ~ N(0,1) with 8 outlier channels x20, B = 4096x4096 bf16 ~
-N(0,0.02) (seeded, synthetic); one step = quantize A and B to NVFP4 (E2M1 elements, UE4M3 scale
-per 16 along K, fp32 tensor scale) + the Blackwell-FP4 GDFS emulated GEMM (G=6, F=35, GS=16,
-KT=64) with fp32 output, bit-exact with TriCast's reference backend.
+Headline workload: the NVFP4 W4A4 emulated GEMM. A = 2048x4096 bf16 ~ N(0,1) with 8 outlier
+channels x20, B = 4096x4096 bf16 ~ N(0,0.02) (seeded, synthetic); one step = quantize A and B to NVFP4
+(E2M1 elements, UE4M3 scale per 16 along K, fp32 tensor scale) + the Blackwell-FP4 GDFS emulated GEMM
+(G=6, F=35, GS=16, KT=64) with fp32 output, bit-exact with TriCast's reference backend.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-Multi-GPU (torchrun, one rank per GPU): weak scaling by N-column slabs — every rank computes its
-own 4096-column slab of a (4096*N)-row weight against the same A; no collective on the data path.
-``--impl reference`` times the CPU oracle (numpy restatement of TriCast's reference backend) on
-the host cores over a bounded row slab of the same workload.
+Multi-GPU (torchrun, one rank per GPU): strong scaling. The one fixed GEMM is split by N-column
+slabs: rank r quantizes all of A and its slab of B's rows (the slab's amax joins the others' in one
+NCCL all-reduce of a 32-bit word, so the slab quantizes exactly as those rows of the whole B would)
+and computes its [2048, 4096/N] output slab. The FP8 CoFDA GEMM (8192^3) is split the same way
+(``aux_strong``), and the 196-layer error sweep is split by layer.
+
+``--impl reference`` times TriCast's own CPU implementation of the path, its pure-PyTorch reference
+backend (installed under ``baseline/_ref``), on all host cores over a bounded row slab of the same
+workload per step; without that install, the numpy restatement under ``oracle/``.
 """
 
 from __future__ import annotations
@@ -19,6 +23,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -33,129 +38,269 @@ METRIC = "bit-exact emulated GEMM GMAC/s + cast GB/s per B200; 1/2/4/8-GPU layer
 M, N, K = 2048, 4096, 4096
 WORKLOAD = ("cfg2 NVFP4 W4A4 emulated GEMM 2048x4096x4096: quantize A,B (nvfp4) + Blackwell-FP4 GDFS "
             "(G=6,F=35,GS=16,KT=64) fp32 out")
+DATA = "synthetic (seeded N(0,1)/N(0,0.02) bf16, 8 outlier channels x20)"
 L2_FLUSH_BYTES = 512 << 20
-# dram__bytes_read.sum + dram__bytes_write.sum of one gdfs_fp4_tc_kernel<4, 0> launch on cfg2 (the ncu
-# capture summarised in profiles/gdfs_fp4_tc_kernel_cfg2.md).
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) and issue-slot share
+# (smsp__issue_active.avg.pct_of_peak_sustained_active / 100) of one gdfs_fp4_tc_kernel<4, 0> launch
+# on the cfg2 operands, from an ncu --set full capture of this build's kernel.
 GDFS_TRAFFIC_BYTES = 40_630_784 + 2_835_968
-GDFS_ISSUE_UTIL = 0.599  # smsp__issue_active.avg.pct_of_peak_sustained_active / 100, same capture
-
-
+GDFS_ISSUE_UTIL = 0.599
 CFG1_BYTES_PER_ELEM = 4 + 4 + 0.5 + 1 / 32  # fp32 in, fp32 dequant out, E2M1 nibble, E8M0 byte per 32
+REF_SLAB = (64, 1024)  # rows of A x rows of B per CPU sample step (full K)
 
 
-def make_cfg1_input():
-    """cfg1: 4096x4096 fp32 N(0,1), 0.1% of entries x50, seed 0 (the benchmark's MXFP4 cast input)."""
+def tricast_module():
+    """TriCast from ``baseline/_ref`` (offline ``pip --target`` install), or None."""
+    ref = ROOT / "baseline" / "_ref"
+    if ref.is_dir() and str(ref) not in sys.path:
+        sys.path.append(str(ref))
+    try:
+        import tricast
+
+        return tricast
+    except ImportError:
+        return None
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
+def measured_peaks() -> dict:
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "sm_max_mhz": 1965.0, "fallback": True}
+
+
+def _smi_sampler(stop: threading.Event, samples: list, index: int) -> None:
+    q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    try:
+        proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200",
+                                 "-i", str(index)], stdout=subprocess.PIPE, text=True)
+    except OSError:
+        return
+    try:
+        while not stop.is_set():
+            line = proc.stdout.readline()
+            if not line:
+                break
+            samples.append([s.strip() for s in line.split(",")])
+    finally:
+        proc.terminate()
+        proc.wait(timeout=5)
+
+
+def clocks_summary(samples: list) -> dict:
+    if not samples:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+    sm = [float(s[1]) for s in samples if s[1].replace(".", "").isdigit()]
+    mx = [float(s[2]) for s in samples if s[2].replace(".", "").isdigit()]
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    reasons = sorted({names[i] for s in samples for i in range(4) if len(s) > 5 + i and s[5 + i].lower() == "active"})
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons, "samples": len(samples)}
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms while the ``with`` block runs."""
+
+    def __init__(self, index: int):
+        self.index, self.samples, self.stop = index, [], threading.Event()
+
+    def __enter__(self):
+        self.thread = threading.Thread(target=_smi_sampler, args=(self.stop, self.samples, self.index), daemon=True)
+        self.thread.start()
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.stop.set()
+        self.thread.join(timeout=5)
+        return False
+
+    def summary(self) -> dict:
+        return clocks_summary(self.samples)
+
+
+def event_pair():
     import torch
 
-    g = torch.Generator().manual_seed(0)
-    x = torch.randn(4096, 4096, generator=g)
-    idx = torch.randperm(4096 * 4096, generator=g)[:16777]
-    x.view(-1)[idx] *= 50
-    return x
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
-def measure_cfg1(dev, steps: int, warmup: int) -> dict:
-    """MXFP4 quantize-dequantize cast of cfg1 with BASELINE's outputs (dequant fp32, packed E2M1
-    codes, E8M0 scale bytes); inputs resident, outputs preallocated (QuantizePlan), L2 flushed
-    between launches, CUDA-event timed."""
+def stats_ms(times: list) -> dict:
+    s = sorted(times)
+    return {"median": statistics.median(s), "mean": sum(s) / len(s), "p99": s[min(len(s) - 1, int(0.99 * len(s)))],
+            "n": len(s)}
+
+
+# --------------------------------------------------------------------------------------------- cfg1
+def measure_cfg1(dev, steps: int, warmup: int, sets: int = 4) -> dict:
+    """MXFP4 quantize-dequantize cast of cfg1 with the benchmark's outputs (dequant fp32, packed E2M1
+    codes, E8M0 scale bytes) through preallocated plans (``QuantizePlan``), CUDA-event timed per
+    launch. Main protocol: ``sets`` copies of the input and of the outputs are used in rotation, back
+    to back, so every launch reads an input and writes outputs that were last touched ``sets`` launches
+    (over 500 MB of traffic) earlier: nothing of them is left in the 126 MB L2, and each launch pays,
+    as in a streaming steady state, for the write-back of the dirty lines the launch before it left.
+    A plain device copy of the input (read 4 B + write 4 B per element) under the same protocol is
+    reported beside it. For comparison, ``write_flush`` repeats both after filling a 512 MiB buffer
+    before each launch (the launch then also pays for writing back the flush's dirty lines)."""
     import torch
 
-    from tricast_b200 import QuantizePlan
+    from tricast_b200 import QuantizePlan, workloads
     from tricast_b200.spec import SCHEMES
 
-    x = make_cfg1_input().to(dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    x0 = workloads.cfg1_input().to(dev)
     spec = SCHEMES["mxfp4"]
     stream = torch.cuda.current_stream(dev)
-    plan = QuantizePlan(x.shape, x.dtype, dev, spec, want_values=False, want_codes=True, want_scale_codes=True,
-                        want_dequant=True)
+    xs = [x0] + [x0.clone() for _ in range(sets - 1)]
+    plans = [QuantizePlan(x0.shape, x0.dtype, dev, spec, want_values=False, want_codes=True, want_scale_codes=True,
+                          want_dequant=True) for _ in range(sets)]
+    ys = [torch.empty_like(x0) for _ in range(sets)]
 
-    def run():
-        return plan.run(x)
+    def rotating(fn) -> list:
+        for i in range(warmup):
+            fn(i % sets)
+        events = []
+        for i in range(steps * sets):
+            e0, e1 = event_pair()
+            e0.record(stream)
+            fn(i % sets)
+            e1.record(stream)
+            events.append((e0, e1))
+        torch.cuda.synchronize(dev)
+        return [a.elapsed_time(b) for a, b in events]
 
-    for _ in range(warmup):
-        run()
-    times = []
-    for _ in range(steps):
-        flush.fill_(1)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        run()
-        e1.record(stream)
-        e1.synchronize()
-        times.append(e0.elapsed_time(e1))
-    t = sum(times) / len(times)
-    # The same protocol around a plain device copy of x (4 + 4 bytes per element): the practical
-    # ceiling of a short streaming kernel, reported beside the STREAM-measured peak.
-    y = torch.empty_like(x)
-    copy_times = []
-    for i in range(warmup + steps):
-        flush.fill_(1)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        y.copy_(x)
-        e1.record(stream)
-        e1.synchronize()
-        if i >= warmup:
-            copy_times.append(e0.elapsed_time(e1))
-    tc = sum(copy_times) / len(copy_times)
-    gbs = x.numel() * CFG1_BYTES_PER_ELEM / (t * 1e-3) / 1e9
+    def flushed(fn) -> list:
+        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        times = []
+        for i in range(warmup + steps):
+            flush.fill_(1)
+            e0, e1 = event_pair()
+            e0.record(stream)
+            fn(0)
+            e1.record(stream)
+            e1.synchronize()
+            if i >= warmup:
+                times.append(e0.elapsed_time(e1))
+        del flush
+        return times
+
+    cast = lambda i: plans[i].run(xs[i])  # noqa: E731
+    copy = lambda i: ys[i].copy_(xs[i])  # noqa: E731
+    t = stats_ms(rotating(cast))["mean"]
+    tc = stats_ms(rotating(copy))["mean"]
+    tf, tcf = stats_ms(flushed(cast))["mean"], stats_ms(flushed(copy))["mean"]
+    nbytes = x0.numel() * CFG1_BYTES_PER_ELEM
+    gbs = nbytes / (t * 1e-3) / 1e9
     hbm = measured_peaks().get("hbm_gbs", 6650.0)
     return {"workload": "cfg1 MXFP4 quantize-dequantize 4096x4096 fp32 (dequant fp32 + packed E2M1 + E8M0 bytes)",
-            "gbs": gbs, "ms": t, "bytes_per_elem": CFG1_BYTES_PER_ELEM, "hbm_frac": gbs / hbm,
-            "hbm_peak_gbs": hbm, "copy_same_protocol_gbs": x.numel() * 8 / (tc * 1e-3) / 1e9,
-            "copy_same_protocol_ms": tc}
+            "gbs": gbs, "ms": t, "bytes_per_elem": CFG1_BYTES_PER_ELEM, "hbm_frac": gbs / hbm, "hbm_peak_gbs": hbm,
+            "protocol": f"{sets} rotating input/output sets back to back ({sets * 136} MB > L2)",
+            "copy_same_protocol_gbs": x0.numel() * 8 / (tc * 1e-3) / 1e9, "copy_same_protocol_ms": tc,
+            "write_flush": {"gbs": nbytes / (tf * 1e-3) / 1e9, "ms": tf,
+                            "copy_gbs": x0.numel() * 8 / (tcf * 1e-3) / 1e9}}
 
 
-def measure_gemm_config(dev, name: str, steps: int, warmup: int, size: int = 0) -> dict:
-    """Device-resident step of cfg3 (FP8 E4M3 W8A8, Hopper CoFDA F=13 CS=32, 8192^3) or cfg4
-    (INT8 per-token x INT4 g128 asymmetric, CoFDA F=23 promoted every 128, 4096x12288x4096):
-    quantize both operands + emulated GEMM, L2 flushed between steps, CUDA-event timed. ``size``
-    (cfg3 only, profiling) replaces 8192 by a smaller cube."""
-    import torch
+# ------------------------------------------------------------------------------- GEMM steps (sharded)
+def gemm_step(name: str, dev, world: int = 1, rank: int = 0, size: int = 0):
+    """(step, macs_whole_job, shape) of one config's step on this rank: quantize all of A and this
+    rank's N-column slab of B (against the whole B's amax where the scheme needs it), then the emulated
+    GEMM of the slab. At world 1 the slab is all of B. ``size`` (cfg3 only) runs a smaller cube."""
+    from tricast_b200 import as_operand, gemm_triton, quantize_triton, workloads
+    from tricast_b200.shard import column_slab, quantize_shard
+    from tricast_b200.spec import PRESETS, SCHEMES
 
-    from tricast_b200 import as_operand, gemm_triton, quantize_triton
-    from tricast_b200.formats import FP16, IntFormat
-    from tricast_b200.operand import Operand
-    from tricast_b200.spec import PRESETS, SCHEMES, MMASpec
-
-    g = torch.Generator().manual_seed(0)
-    if name == "cfg3":
-        m = n = k = size or 8192
-        a = torch.randn(m, k, generator=g).bfloat16().to(dev)
-        b = (torch.randn(n, k, generator=g) * 0.02).bfloat16().to(dev)
+    if name == "cfg2":
+        a_cpu, b_cpu = workloads.cfg2_inputs()
+        scheme_a = scheme_b = SCHEMES["nvfp4"]
+        spec = PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32")
+    elif name == "cfg3":
+        a_cpu, b_cpu = workloads.cfg3_inputs(size)
+        scheme_a = scheme_b = SCHEMES["fp8_tensor"]
         spec = PRESETS["nvidia_hopper_fp8"].with_(out_format="fp32")
-
-        def step():
-            qa, qb = quantize_triton(a, SCHEMES["fp8_tensor"]), quantize_triton(b, SCHEMES["fp8_tensor"])
-            return gemm_triton(as_operand(qa, compact=True), as_operand(qb, compact=True), spec)
     else:
-        m, n, k = 4096, 12288, 4096
-        x = torch.randn(m, k, generator=g).to(dev)
-        w = (torch.randn(n, k, generator=g) * 0.02).to(dev)
-        spec = MMASpec("cofda", f_bits=23, chunk_size=32, promote_interval=128, out_format="fp32")
-        int5 = IntFormat("int5", 5)
+        a_cpu, b_cpu = workloads.cfg4_inputs()
+        scheme_a, scheme_b = SCHEMES["int8_row"], SCHEMES["int4_g128_zp"]
+        spec = workloads.cfg4_spec()
+    m, k = a_cpu.shape
+    n = b_cpu.shape[0]
+    s, e = column_slab(n, world, rank)
+    a, b = a_cpu.to(dev), b_cpu[s:e].contiguous().to(dev)
 
-        def step():
-            qa = quantize_triton(x, SCHEMES["int8_row"])
-            qw = quantize_triton(w, SCHEMES["int4_g128_zp"])
-            bvals = qw.values.float() - qw.zero_point.repeat_interleave(128, dim=1)
-            return gemm_triton(as_operand(qa, compact=True), Operand(bvals, int5, qw.scale, FP16, "k", 128), spec)
+    def operands(xa=a, xb=b):
+        qa = quantize_triton(xa, scheme_a)
+        qb = quantize_shard(xb, scheme_b)
+        if name == "cfg4":
+            return workloads.cfg4_operands(qa, qb)
+        return as_operand(qa, compact=True), as_operand(qb, compact=True)
+
+    def gemm(opa, opb):
+        return gemm_triton(opa, opb, spec)
+
+    def step(xa=a, xb=b):
+        return gemm(*operands(xa, xb))
+
+    step.operands, step.gemm = operands, gemm
+    return step, m * n * k, (m, n, k), (a_cpu, b_cpu[s:e].contiguous())
+
+
+def time_steps(step, dev, steps: int, warmup: int, world: int = 1) -> list:
+    """Device time of each of ``steps`` calls (after ``warmup``), a 512 MiB L2 flush before each one
+    outside its events, all enqueued back to back; barrier + synchronize on both sides."""
+    import torch
+    import torch.distributed as dist
+
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     for _ in range(warmup):
         step()
-    times = []
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    events = []
     for _ in range(steps):
         flush.fill_(1)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, e1 = event_pair()
         e0.record(stream)
         step()
         e1.record(stream)
-        e1.synchronize()
-        times.append(e0.elapsed_time(e1))
-    t = sum(times) / len(times)
-    return {"workload": name, "shape": [m, n, k], "gmacs": m * n * k / (t * 1e-3) / 1e9, "ms": t}
+        events.append((e0, e1))
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    return [a.elapsed_time(b) for a, b in events]
+
+
+def max_over_ranks(values: list, dev, world: int) -> list:
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(values, dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def measure_gemm_config(dev, name: str, steps: int, warmup: int, world: int = 1, rank: int = 0,
+                        size: int = 0) -> dict:
+    """Device-timed step of cfg3 (FP8 E4M3 W8A8, Hopper CoFDA F=13 CS=32, 8192^3) or cfg4 (INT8 per
+    token x INT4 g128 asymmetric, CoFDA F=23 promoted every 128, 4096x12288x4096), split by N-column
+    slabs over the ranks (whole job, max over ranks)."""
+    step, macs, shape, _ = gemm_step(name, dev, world, rank, size)
+    t = statistics.mean(time_steps(step, dev, steps, warmup, world))
+    (t,) = max_over_ranks([t], dev, world)
+    return {"workload": name, "shape": list(shape), "n_gpus": world, "gmacs": macs / (t * 1e-3) / 1e9, "ms": t,
+            "split": "N-column slabs" if world > 1 else "none"}
 
 
 def measure_decode(dev, calls: int = 200) -> list:
@@ -195,196 +340,239 @@ def measure_decode(dev, calls: int = 200) -> list:
         times = []
         for _ in range(20):
             flush.fill_(1)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0, e1 = event_pair()
             e0.record(stream)
             graph.replay()
             e1.record(stream)
             e1.synchronize()
             times.append(e0.elapsed_time(e1) * 1e3)
         del graph
-        times.sort()
         out.append({"workload": f"decode M=1 {scheme} x {preset} 1x4096x4096 (quantize activation + GEMM)",
-                    "call_us": call_us, "gpu_us": times[len(times) // 2]})
+                    "call_us": call_us, "gpu_us": statistics.median(times)})
     return out
 
 
-def measure_cfg2_step(dev, steps: int, warmup: int) -> dict:
-    """The headline step alone (quantize A and B to NVFP4 + Blackwell-FP4 GEMM, inputs resident, L2
-    flushed between steps): a short, focused run for profilers."""
+# ------------------------------------------------------------------ TriCast's own GPU backend (Triton)
+def measure_tricast_triton(dev, ours_cfg2=None) -> dict:
+    """TriCast's unmodified Triton backend (``backend="triton"``: ``kernels/quantize.py:192-275``,
+    ``kernels/mma.py:821-886``) on this GPU, through its public API, timed with its own protocol
+    (``scripts/bench/bench_mma_vs_nadpe.py:47-69``: 3 warm-ups, 5 CUDA-event timed calls; median, mean,
+    p99), plus a 512 MiB L2 flush before each timed call as in this benchmark. The first call of each
+    config (Triton JIT) is outside the timing. cfg2's output is compared bit for bit with this
+    library's."""
     import torch
 
-    from tricast_b200 import as_operand, gemm_triton, quantize_triton
-    from tricast_b200.spec import PRESETS, SCHEMES
+    if tricast_module() is None:
+        return {"unavailable": "TriCast is not installed under baseline/_ref"}
+    from tricast.mma.api import gemm
+    from tricast.quant.api import quantize
 
-    a_cpu, b_cpu = make_inputs(0)
-    a, b = a_cpu.to(dev), b_cpu.to(dev)
-    spec_q, spec_m = SCHEMES["nvfp4"], PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32")
+    from tricast_b200 import workloads
+
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream(dev)
 
-    def step():
-        qa, qb = quantize_triton(a, spec_q), quantize_triton(b, spec_q)
-        return gemm_triton(as_operand(qa, compact=True), as_operand(qb, compact=True), spec_m)
+    def timed(fn, warmup: int = 3, repeat: int = 5) -> list:
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        times = []
+        for _ in range(repeat):
+            flush.fill_(1)
+            e0, e1 = event_pair()
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            times.append(e0.elapsed_time(e1))
+        return times
 
-    for _ in range(warmup):
-        step()
-    times = []
-    for _ in range(steps):
-        flush.fill_(1)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        step()
-        e1.record(stream)
-        e1.synchronize()
-        times.append(e0.elapsed_time(e1))
-    t = sum(times) / len(times)
-    m, n, k = a.shape[0], b.shape[0], a.shape[1]
-    return {"workload": "cfg2 step", "shape": [m, n, k], "gmacs": m * n * k / (t * 1e-3) / 1e9, "ms": t}
-
-
-def make_inputs(rank: int):
-    """cfg2 operands, generated seeded on the CPU so every GPU count sees identical tensors."""
-    import torch
-
-    g = torch.Generator().manual_seed(0)
-    a = torch.randn(M, K, generator=g)
-    a[:, torch.randperm(K, generator=g)[:8]] *= 20
-    gb = torch.Generator().manual_seed(1000 + rank)
-    b = torch.randn(N, K, generator=gb) * 0.02
-    return a.bfloat16(), b.bfloat16()
-
-
-def _smi_sampler(stop: threading.Event, samples: list, index: int) -> None:
-    q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    out = {"protocol": "TriCast timed(): 3 warm-ups + 5 CUDA-event timed calls, L2 flushed before each"}
     try:
-        proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200",
-                                 "-i", str(index)], stdout=subprocess.PIPE, text=True)
-    except OSError:
-        return
-    try:
-        while not stop.is_set():
-            line = proc.stdout.readline()
-            if not line:
-                break
-            samples.append([s.strip() for s in line.split(",")])
-    finally:
-        proc.terminate()
-        proc.wait(timeout=5)
+        x = workloads.cfg1_input().to(dev)
+        quantize(x, "mxfp4", backend="triton")
+        t = stats_ms(timed(lambda: quantize(x, "mxfp4", backend="triton")))
+        out["cfg1_quantize_mxfp4"] = {**t, "gbs_6.125B_per_elem": x.numel() * 6.125 / (t["median"] * 1e-3) / 1e9}
+    except Exception as exc:  # a JIT or launch failure is reported, not fatal
+        out["cfg1_quantize_mxfp4"] = {"error": repr(exc)[:300]}
+    for name, scheme, preset, size in (("cfg2", "nvfp4", "nvidia_blackwell_fp4", 0),
+                                       ("cfg3", "fp8_tensor", "nvidia_hopper_fp8", 0)):
+        try:
+            a_cpu, b_cpu = workloads.cfg2_inputs() if name == "cfg2" else workloads.cfg3_inputs(size)
+            a, b = a_cpu.to(dev), b_cpu.to(dev)
+            spec = {"preset": preset, "out_format": "fp32"}
+
+            def step():
+                qa, qb = quantize(a, scheme, backend="triton"), quantize(b, scheme, backend="triton")
+                return gemm(qa, qb, spec, backend="triton")
+
+            first = step()
+            rec = {}
+            if name == "cfg2" and ours_cfg2 is not None:
+                mine = ours_cfg2()
+                rec["bits_differ_from_b200"] = int((first.view(torch.int32) != mine.view(torch.int32)).sum())
+            del first
+            t = stats_ms(timed(step, 1 if name == "cfg3" else 3, 3 if name == "cfg3" else 5))
+            macs = a.shape[0] * b.shape[0] * a.shape[1]
+            rec.update({**t, "gmacs": macs / (t["median"] * 1e-3) / 1e9, "shape": [a.shape[0], b.shape[0], a.shape[1]]})
+            out[f"{name}_step"] = rec
+        except Exception as exc:
+            out[f"{name}_step"] = {"error": repr(exc)[:300]}
+    return out
 
 
-def clocks_summary(samples: list) -> dict:
-    if not samples:
-        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-    sm = [float(s[1]) for s in samples if s[1].replace(".", "").isdigit()]
-    mx = [float(s[2]) for s in samples if s[2].replace(".", "").isdigit()]
-    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-    reasons = sorted({names[i] for s in samples for i in range(4) if len(s) > 5 + i and s[5 + i].lower() == "active"})
-    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-            "reasons": reasons, "samples": len(samples)}
+# ------------------------------------------------------------------------------- the CPU reference
+class CpuSample:
+    """One bounded sample of the cfg2 step on the host cores: a ``rows`` x ``cols`` slab of the output
+    with the whole K (rows of A, rows of B), its operands quantized from the slab rows, then the
+    emulated GEMM. ``kind`` "reference": TriCast's pure-PyTorch reference backend from ``baseline/_ref``
+    (``backend="reference"``, ``src/tricast/reference/{quantize,mma}.py``) with every host thread;
+    "port": the numpy restatement under ``oracle/`` on one core, when TriCast is not installed. Every
+    output is computed independently (``reference/mma.py:340``), so slab throughput is whole-job
+    throughput."""
+
+    def __init__(self, rows: int, cols: int):
+        import torch
+
+        from tricast_b200 import workloads
+
+        a, b = workloads.cfg2_inputs()
+        self.a, self.b = a[:rows].float(), b[:cols].float()
+        self.rows, self.cols = rows, cols
+        self.tricast = tricast_module()
+        self.kind = "reference" if self.tricast is not None else "port"
+        self.threads = os.cpu_count() or 1
+        if self.kind == "reference":
+            torch.set_num_threads(self.threads)
+        else:
+            self.threads = 1
+
+    def describe(self) -> str:
+        what = "TriCast reference backend (pure PyTorch)" if self.kind == "reference" else "numpy oracle port"
+        return (f"{what}: {self.rows}x{self.cols}x{K} slab of cfg2 per step (quantize both slabs nvfp4 + "
+                f"Blackwell-FP4 GDFS, fp32 out), {self.threads} threads on {cpu_model()}")
+
+    def run(self) -> int:
+        if self.kind == "reference":
+            from tricast.mma.api import gemm
+            from tricast.quant.api import quantize
+
+            qa = quantize(self.a, "nvfp4", backend="reference")
+            qb = quantize(self.b, "nvfp4", backend="reference")
+            gemm(qa, qb, {"preset": "nvidia_blackwell_fp4", "out_format": "fp32"}, backend="reference")
+        else:
+            import numpy as np
+
+            import oracle
+            from oracle.quantize import quantize_reference
+            from tricast_b200.spec import PRESETS, SCHEMES
+
+            spec = SCHEMES["nvfp4"]
+            qa, qb = quantize_reference(self.a.numpy(), spec), quantize_reference(self.b.numpy(), spec)
+
+            class Op:
+                def __init__(self, q):
+                    self.values, self.fmt, self.scale = q.values, spec.format, q.scale
+                    self.scale_fmt, self.scale_kind, self.k_domain = spec.scale.format, "k", 16
+                    self.alpha = np.float32(q.global_scale)
+
+            oracle.gemm_reference(Op(qa), Op(qb), PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32"))
+        return self.rows * self.cols * K
 
 
-def measured_peaks() -> dict:
-    try:
-        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except (OSError, ValueError):
-        return {"hbm_gbs": 6650.0, "sm_max_mhz": 1965.0, "fallback": True}
-
-
-def cpu_oracle_sample(rows: int, cols: int, seed_rank: int = 0) -> tuple[float, str]:
-    """Oracle (numpy restatement of TriCast's reference backend) on a row x column slab with the
-    full K: quantize the slab of A and B, then the emulated GEMM. Returns (GMAC/s, description)."""
-    import numpy as np
-
-    import oracle
-    from oracle.quantize import quantize_reference
-    from tricast_b200.spec import PRESETS, SCHEMES
-
-    a, b = make_inputs(seed_rank)
-    a = a[:rows].float().numpy()
-    b = b[:cols].float().numpy()
-    spec = SCHEMES["nvfp4"]
+def cpu_baseline() -> dict:
+    sample = CpuSample(*REF_SLAB)
+    sample.run()  # warm-up
     t0 = time.perf_counter()
-    qa, qb = quantize_reference(a, spec), quantize_reference(b, spec)
-
-    class Op:
-        def __init__(self, q):
-            self.values, self.fmt, self.scale = q.values, spec.format, q.scale
-            self.scale_fmt, self.scale_kind, self.k_domain = spec.scale.format, "k", 16
-            self.alpha = np.float32(q.global_scale)
-
-    oracle.gemm_reference(Op(qa), Op(qb), PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32"))
+    macs = sample.run()
     dt = time.perf_counter() - t0
-    return rows * cols * K / dt / 1e9, f"{rows}x{cols}x{K} slab (quantize both + GDFS GEMM), {dt:.2f}s"
-
-
-_WORKER = {}
-
-
-def _init_worker(rows: int, cols: int) -> None:
-    """Pool initializer: the seeded inputs are generated once per worker process."""
-    a, b = make_inputs(0)
-    _WORKER["a"], _WORKER["b"] = a.float().numpy(), b[:cols].float().numpy()
-    _WORKER["rows"] = rows
-
-
-def _slab_worker(offset: int) -> int:
-    import numpy as np
-
-    import oracle
-    from oracle.quantize import quantize_reference
-    from tricast_b200.spec import PRESETS, SCHEMES
-
-    rows = _WORKER["rows"]
-    a = _WORKER["a"][offset:offset + rows]
-    b = _WORKER["b"]
-    spec = SCHEMES["nvfp4"]
-    qa, qb = quantize_reference(a, spec), quantize_reference(b, spec)
-
-    class Op:
-        def __init__(self, q):
-            self.values, self.fmt, self.scale = q.values, spec.format, q.scale
-            self.scale_fmt, self.scale_kind, self.k_domain = spec.scale.format, "k", 16
-            self.alpha = np.float32(q.global_scale)
-
-    oracle.gemm_reference(Op(qa), Op(qb), PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32"))
-    return rows * b.shape[0] * K
+    return {"value": macs / dt / 1e9, "unit": "GMAC/s", "cores": sample.threads, "kind": sample.kind,
+            "sample": f"{sample.describe()}; {dt:.2f} s"}
 
 
 def run_reference(args) -> None:
-    """CPU reference arm: the oracle port on all host cores, each step a bounded slab."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    """The reference arm: TriCast's CPU implementation on the host cores, rank 0 only, each step one
+    bounded slab of the cfg2 workload."""
+    if int(os.environ.get("RANK", "0")) != 0:
         return
-    import multiprocessing as mp
-
-    cores = os.cpu_count() or 1
-    rows_per_worker, cols = 8, 1024
-    jobs = [i * rows_per_worker for i in range(cores)]
-    ctx = mp.get_context("spawn")
-    with ctx.Pool(cores, initializer=_init_worker, initargs=(rows_per_worker, cols)) as pool:
-        for _ in range(args.warmup):
-            pool.map(_slab_worker, jobs[:1])
-        times = []
-        macs = 0
-        for _ in range(args.steps):
-            t0 = time.perf_counter()
-            macs = sum(pool.map(_slab_worker, jobs))
-            times.append(time.perf_counter() - t0)
+    sample = CpuSample(*REF_SLAB)
+    for _ in range(args.warmup):
+        sample.run()
+    times, macs = [], 0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        macs = sample.run()
+        times.append(time.perf_counter() - t0)
     total = sum(times)
     value = macs * args.steps / total / 1e9
-    sample = f"{cores} workers x ({rows_per_worker}x{cols}x{K} slab: quantize both + GDFS GEMM) per step"
     line = {"metric": METRIC, "value": value, "unit": "GMAC/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64",
-            "data": "synthetic (seeded N(0,1)/N(0,0.02) bf16, 8 outlier channels x20)",
-            "config": {"workload": WORKLOAD, "global_batch": M, "sample": sample, "l2": "n/a (CPU)"},
-            "cpu_baseline": {"value": value, "unit": "GMAC/s", "cores": cores, "kind": "port", "sample": sample},
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int64", "data": DATA,
+            "config": {"workload": WORKLOAD, "global_batch": M, "sample": sample.describe(), "l2": "n/a (CPU)"},
+            "cpu_baseline": {"value": value, "unit": "GMAC/s", "cores": sample.threads, "kind": sample.kind,
+                             "sample": sample.describe()},
             "e2e": {"value": value, "unit": "GMAC/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------ end to end
+def e2e_pipelined(step, host_inputs, dev, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
+    """The step end to end from pinned host memory, as a serving loop runs it: every step copies its
+    inputs host -> device (a copy stream), runs the public-API step (the compute stream) and copies its
+    result device -> host (a third stream). Two device input buffers and two pinned host output
+    buffers alternate, so step i + 1's upload and step i - 1's download overlap step i's compute; the
+    ordering is by CUDA events only. Returns (ms per step over the K timed steps, from the first
+    upload's start to the last download's end; H2D bytes per step; D2H bytes per step)."""
+    import torch
+    import torch.distributed as dist
+
+    comp = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    dev_in = [[torch.empty_like(h, device=dev) for h in host_inputs] for _ in range(2)]
+    host_out = [None, None]
+    in_ready = [torch.cuda.Event(), torch.cuda.Event()]
+    in_free = [torch.cuda.Event(), torch.cuda.Event()]
+    d2h_bytes = 0
+
+    def run(n: int) -> None:
+        nonlocal d2h_bytes
+        for i in range(n):
+            j = i & 1
+            if i >= 2:
+                up.wait_event(in_free[j])
+            with torch.cuda.stream(up):
+                for d, h in zip(dev_in[j], host_inputs):
+                    d.copy_(h, non_blocking=True)
+                in_ready[j].record(up)
+            comp.wait_event(in_ready[j])
+            out = step(*dev_in[j])
+            in_free[j].record(comp)
+            done = torch.cuda.Event()
+            done.record(comp)
+            if host_out[j] is None:
+                host_out[j] = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+            down.wait_event(done)
+            with torch.cuda.stream(down):
+                host_out[j].copy_(out, non_blocking=True)
+            out.record_stream(down)
+            d2h_bytes = out.numel() * out.element_size()
+
+    run(warmup)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    start, end = event_pair()
+    start.record(up)
+    run(steps)
+    down.wait_stream(up)
+    end.record(down)
+    end.synchronize()
+    torch.cuda.synchronize(dev)
+    h2d = sum(h.numel() * h.element_size() for h in host_inputs)
+    return start.elapsed_time(end) / steps, h2d, d2h_bytes
+
+
+# ------------------------------------------------------------------------------------ the headline
 def run_b200(args) -> None:
     import torch
     import torch.distributed as dist
@@ -399,139 +587,119 @@ def run_b200(args) -> None:
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
-    from tricast_b200 import _native, as_operand, gemm_triton, quantize_triton
-    from tricast_b200.spec import PRESETS, SCHEMES
+    from tricast_b200 import _native
+    from tricast_b200.sweep import SweepConfig, measure_costs, run_sweep
 
     lib = _native.lib()
-    spec_q = SCHEMES["nvfp4"]
-    spec_m = PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32")
-    a_cpu, b_cpu = make_inputs(rank)
-    a, b = a_cpu.to(dev), b_cpu.to(dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    step, macs, _, host_inputs = gemm_step("cfg2", dev, world, rank)
     stream = torch.cuda.current_stream(dev)
-
     gemm_events = []
 
-    def step(xa, xb, record=False):
-        qa = quantize_triton(xa, spec_q)
-        qb = quantize_triton(xb, spec_q)
-        if record:
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            out = gemm_triton(as_operand(qa, compact=True), as_operand(qb, compact=True), spec_m)
-            e1.record(stream)
-            gemm_events.append((e0, e1))
-        else:
-            out = gemm_triton(as_operand(qa, compact=True), as_operand(qb, compact=True), spec_m)
-        return out
-
-    def barrier():
+    # The headline: K steps enqueued back to back (no host wait per step), each with its own events,
+    # a 512 MiB L2 flush between steps outside them; max over ranks.
+    for _ in range(args.warmup):
+        step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    with Clocks(local) as clocks:
+        launches0 = lib.tc_launch_count()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
+        step_events = []
+        for _ in range(args.steps):
+            flush.fill_(1)
+            s0, s1 = event_pair()
+            s0.record(stream)
+            step()
+            s1.record(stream)
+            step_events.append((s0, s1))
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        launches = lib.tc_launch_count() - launches0
+        # The GEMM call alone (operand encoders + GDFS kernel) on operands quantized beforehand, with
+        # events around it on the stream it launches on.
+        ops = step.operands()
+        for _ in range(args.steps):
+            flush.fill_(1)
+            e0, e1 = event_pair()
+            e0.record(stream)
+            step.gemm(*ops)
+            e1.record(stream)
+            gemm_events.append((e0, e1))
+        torch.cuda.synchronize(dev)
+        del ops
+        # End to end through the public API from pinned host memory.
+        pinned = [h.pin_memory() for h in host_inputs]
+        t_e2e, h2d, d2h = e2e_pipelined(step, pinned, dev, args.steps, args.warmup, world)
+        # Layer sweep (cfg5): per-shape costs measured at full size (which also warms every shape
+        # up), LPT on them, then the device-timed sweep, max over ranks.
+        cfg = SweepConfig()
+        costs = measure_costs(cfg, dev)
+        breakdown = {}
+        _, sweep_secs = run_sweep(cfg, costs=costs, breakdown=breakdown)
+        # The FP8 CoFDA GEMM (cfg3, 8192^3) split the same way as the headline.
+        strong = None if (args.quick and world == 1) else measure_gemm_config(dev, "cfg3", 3, 1, world, rank)
+    step_ms = [a.elapsed_time(b) for a, b in step_events]
+    gemm_ms = [a.elapsed_time(b) for a, b in gemm_events]
 
-    for _ in range(args.warmup):
-        step(a, b)
-    barrier()
-
-    samples: list = []
-    stop = threading.Event()
-    sampler = threading.Thread(target=_smi_sampler, args=(stop, samples, local), daemon=True)
-    sampler.start()
-    time.sleep(0.3)
-    launches0 = lib.tc_launch_count()
-    barrier()
-    # The K steps are enqueued back to back, as a serving loop would issue them (no host wait per
-    # step); each step's device time comes from its own pair of events, read after the final sync.
-    step_events = []
-    for _ in range(args.steps):
-        flush.fill_(1)  # evict A/B/outputs from L2 between steps (outside the step's events)
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record(stream)
-        step(a, b, record=True)
-        s1.record(stream)
-        step_events.append((s0, s1))
-    barrier()
-    step_ms = [s0.elapsed_time(s1) for s0, s1 in step_events]
-    launches = lib.tc_launch_count() - launches0
-
-    # End to end through the public API from pinned host memory: H2D of A and B, quantize + GEMM,
-    # D2H of the fp32 output, all inside the timed region.
-    ha, hb = a_cpu.pin_memory(), b_cpu.pin_memory()
-    hout = torch.empty((M, N), dtype=torch.float32).pin_memory()
-    e2e_ms = []
-    for i in range(args.warmup + args.steps):
-        flush.fill_(1)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        da, db = ha.to(dev, non_blocking=True), hb.to(dev, non_blocking=True)
-        out = step(da, db)
-        hout.copy_(out, non_blocking=True)
-        e1.record(stream)
-        e1.synchronize()
-        if i >= args.warmup:
-            e2e_ms.append(e0.elapsed_time(e1))
-    barrier()
-    stop.set()
-    sampler.join(timeout=5)
-
-    # Layer sweep (cfg5): 196 layers x 4 formats sharded over all ranks, NCCL gather of the metric
-    # sums; a reduced warm-up run first, then the full sweep, device-timed, max over ranks.
-    from tricast_b200.sweep import SweepConfig, run_sweep
-
-    run_sweep(SweepConfig(blocks=1, tokens=256))
-    _, sweep_secs = run_sweep(SweepConfig())
-
-    t_step = sum(step_ms) / len(step_ms)
-    t_gemm = sum(e0.elapsed_time(e1) for e0, e1 in gemm_events) / len(gemm_events)
-    t_e2e = sum(e2e_ms) / len(e2e_ms)
-    stats = torch.tensor([t_step, t_gemm, t_e2e], dtype=torch.float64, device=dev)
+    t_step, t_gemm, t_e2e = max_over_ranks([statistics.mean(step_ms), statistics.mean(gemm_ms), t_e2e], dev, world)
+    sizes = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
     if world > 1:
-        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    t_step, t_gemm, t_e2e = stats.tolist()
-    macs = M * N * K
+        dist.all_reduce(sizes)
+    h2d_all, d2h_all = (int(v) for v in sizes.tolist())
     if rank == 0:
-        clk = clocks_summary(samples)
+        clk = clocks.summary()
         peaks = measured_peaks()
         sm_mhz = clk["sm_mhz"] or peaks.get("sm_max_mhz", 1965.0)
-        # The GDFS FP4 kernel computes every 16-product group sum exactly with four DP4A; its bound is
-        # the integer dot-product rate: 148 SMs x 64 DP4A lanes per clock x 4 MAC x SM clock.
-        dp4a_lanes = 64
-        peak_gmacs = 148 * dp4a_lanes * 4 * sm_mhz * 1e6 / 1e9
-        achieved = macs / (t_gemm * 1e-3) / 1e9
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        # The group dot products are exact integer sums; their bound is the CUDA cores' integer
+        # dot-product rate: SMs x 64 DP4A lanes per clock x 4 MAC x SM clock.
+        peak_gmacs = sms * 64 * 4 * sm_mhz * 1e6 / 1e9
+        rank_macs = macs / world
+        achieved = rank_macs / (t_gemm * 1e-3) / 1e9
         line = {
-            "metric": METRIC, "value": world * macs / (t_step * 1e-3) / 1e9, "unit": "GMAC/s", "n_gpus": world,
+            "metric": METRIC, "value": macs / (t_step * 1e-3) / 1e9, "unit": "GMAC/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int64",
-            "data": "synthetic (seeded N(0,1)/N(0,0.02) bf16, 8 outlier channels x20)",
-            "config": {"workload": WORKLOAD, "global_batch": M * world, "seq_len": K,
-                       "parallelism": f"n-slab x{world} (weak)", "l2": "flushed between steps (512 MiB write)"},
-            "e2e": {"value": world * macs / (t_e2e * 1e-3) / 1e9, "unit": "GMAC/s",
-                    "h2d_bytes_per_step": (M * K + N * K) * 2, "d2h_bytes_per_step": M * N * 4},
+            "scaling": "strong", "vs_baseline": None, "dtype": "int64", "data": DATA,
+            "config": {"workload": WORKLOAD, "global_batch": M, "seq_len": K,
+                       "parallelism": f"N-column slabs x{world} (one fixed GEMM)" if world > 1 else "single GPU",
+                       "l2": "flushed between steps (512 MiB write)"},
+            "e2e": {"value": macs / (t_e2e * 1e-3) / 1e9, "unit": "GMAC/s", "h2d_bytes_per_step": h2d_all,
+                    "d2h_bytes_per_step": d2h_all,
+                    "protocol": "K steps pipelined from pinned host memory: upload, compute and download on three "
+                                "streams with double-buffered inputs and outputs; timed from the first upload to "
+                                "the last download; bytes summed over ranks"},
             "gpu_launches": int(launches),
             "roofline": {"bound": "alu", "achieved": achieved, "peak": peak_gmacs, "unit": "GMAC/s",
-                         "frac": achieved / peak_gmacs, "traffic": GDFS_TRAFFIC_BYTES,
+                         "frac": achieved / peak_gmacs, "traffic": GDFS_TRAFFIC_BYTES if world == 1 else None,
                          "issue_util": GDFS_ISSUE_UTIL,
-                         "note": f"emulated GEMM (encode + GDFS kernel, CUDA events); the group dot products "
-                                 "run on tcgen05 int8 MMAs and the exact int64/fp64 tile arithmetic on the CUDA "
-                                 f"cores bounds the kernel; peak = the CUDA-core DP4A rate, 148 SMs x {dp4a_lanes} "
-                                 f"lanes x 4 MAC x {sm_mhz:.0f} MHz; traffic = DRAM bytes per GDFS launch from one "
-                                 "ncu capture; issue_util = smsp__issue_active of that capture (the issue-slot "
-                                 "share the kernel keeps busy)"},
+                         "note": f"emulated GEMM per rank (operand encoders + GDFS kernel, CUDA events on its stream); "
+                                 "the group dot products run on tcgen05 int8 MMAs and the exact int64/fp64 tile "
+                                 f"arithmetic on the CUDA cores bounds the kernel; peak = {sms} SMs x 64 DP4A lanes x "
+                                 f"4 MAC x {sm_mhz:.0f} MHz (sampled); traffic and issue_util: DRAM bytes and "
+                                 "issue-slot share of one GDFS launch on cfg2 from one ncu capture"},
             "gemm_ms": t_gemm,
             "aux_sweep": {"workload": "cfg5 per-layer error sweep: 196 Qwen3-0.6B-shaped layers x "
                                       "(MXFP4, NVFP4, FP8 E4M3, INT4-g128) vs fp64, 2048 tokens",
-                          "secs": sweep_secs, "n_gpus": world, "sharding": "LPT by layer MACs",
+                          "secs": sweep_secs, "n_gpus": world, "sharding": "LPT on measured per-shape layer time",
+                          "per_rank": breakdown, "layer_cost_s": {f"{a}x{b}": v for (a, b), v in costs.items()},
                           "collective": "NCCL all_gather of [layers, 4, 6] fp64 metric sums"},
             "clocks": clk,
         }
+        if strong is not None:
+            line["aux_strong"] = strong
         if world == 1:
             line["aux_cast"] = measure_cfg1(dev, args.steps, args.warmup)
-            line["aux_gemm"] = [measure_gemm_config(dev, c, max(2, args.steps // 3), 1) for c in ("cfg3", "cfg4")]
+            line["aux_gemm"] = [measure_gemm_config(dev, "cfg4", max(3, args.steps // 3), 1)]
             line["aux_decode"] = measure_decode(dev)
-        if world == 1 and not args.no_cpu_baseline:
-            v, desc = cpu_oracle_sample(32, 512)
-            line["cpu_baseline"] = {"value": v, "unit": "GMAC/s", "cores": 1, "kind": "port", "sample": desc}
+            if not args.quick:
+                line["aux_triton"] = measure_tricast_triton(dev, step)
+            if not args.no_cpu_baseline:
+                line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -545,28 +713,34 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg2step", "cfg1", "cfg3", "cfg4", "decode"],
-                    help="cfg2step/cfg1/cfg3/cfg4/decode run only that measurement (for profiling)")
+    ap.add_argument("--quick", action="store_true", help="skip the slow auxiliary measurements (Triton, cfg3)")
+    ap.add_argument("--workload", default="all", choices=["all", "cfg2step", "cfg1", "cfg3", "cfg4", "decode", "triton"],
+                    help="run only that measurement on one GPU (for profiling)")
     ap.add_argument("--cube", type=int, default=0,
                     help="with --workload cfg3: run an M = N = K = CUBE case instead of 8192 (profiling)")
     args = ap.parse_args()
-    if args.workload != "cfg2" and args.impl != "reference":
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    if args.workload != "all":
         import torch
 
         dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
         if args.workload == "cfg1":
             print(json.dumps(measure_cfg1(dev, args.steps, args.warmup)))
         elif args.workload == "cfg2step":
-            print(json.dumps(measure_cfg2_step(dev, args.steps, args.warmup)))
+            step, macs, shape, _ = gemm_step("cfg2", dev)
+            t = statistics.mean(time_steps(step, dev, args.steps, args.warmup))
+            print(json.dumps({"workload": "cfg2 step", "shape": list(shape), "ms": t, "gmacs": macs / (t * 1e-3) / 1e9}))
         elif args.workload == "decode":
             print(json.dumps(measure_decode(dev, calls=args.steps)))
+        elif args.workload == "triton":
+            print(json.dumps(measure_tricast_triton(dev)))
         else:
-            print(json.dumps(measure_gemm_config(dev, args.workload, args.steps, args.warmup, args.cube)))
+            print(json.dumps(measure_gemm_config(dev, args.workload, args.steps, args.warmup, size=args.cube)))
         return
-    if args.impl == "reference":
-        run_reference(args)
-    else:
-        run_b200(args)
+    run_b200(args)
 
 
 if __name__ == "__main__":
