@@ -701,6 +701,9 @@ def run_b200(args) -> None:
             if not args.no_cpu_baseline:
                 line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
+    from tricast_b200.sweep import release_graphs
+
+    release_graphs()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

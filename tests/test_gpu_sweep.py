@@ -94,3 +94,20 @@ def test_sweep_resume_skips_recorded_layers(tmp_path):
     second, _ = run_sweep(cfg, out_dir=str(tmp_path))
     assert [f.stat().st_mtime_ns for f in files] == stamp  # nothing recomputed or rewritten
     assert first == second
+
+
+def test_graph_replay_equals_eager_pass():
+    """Each layer replayed from its shape's captured graph (static buffers refilled per layer) gives the
+    eager pass's sums; layers of one shape share one graph."""
+    from tricast_b200.sweep import _GRAPHS, release_graphs, run_layers
+
+    cfg = SweepConfig(blocks=2, tokens=64, hidden_scale=8)
+    dev = torch.device("cuda", 0)
+    release_graphs()
+    graphed = run_layers(cfg.layers(), cfg, dev, graphs=True)
+    assert len(_GRAPHS) == 5  # distinct (in, out) shapes of the 14 layers
+    eager = run_layers(cfg.layers(), cfg, dev, graphs=False)
+    torch.cuda.synchronize()
+    assert torch.allclose(graphed, eager, rtol=1e-12, atol=0)
+    assert torch.equal(graphed[..., 4], eager[..., 4])  # the max is order-free
+    release_graphs()

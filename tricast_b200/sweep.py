@@ -154,8 +154,69 @@ def measure_costs(cfg: SweepConfig, device, repeats: int = 2) -> dict:
     return table
 
 
-def run_layers(entries: list, cfg: SweepConfig, device, out_dir: str | None = None) -> torch.Tensor:
-    """Metric sums [len(entries), len(FORMATS), 6] (fp64, on the device) for this rank's layers."""
+def layer_sums(x: torch.Tensor, w: torch.Tensor, sums: torch.Tensor) -> None:
+    """One layer's work: the fp64 reference output, the four emulated outputs and their error sums,
+    added into ``sums`` [formats, 6]."""
+    ref = reference(x, w)
+    for col, fmt in enumerate(FORMATS):
+        stats = ErrorStats(x.device)
+        stats.sums = sums[col]
+        stats.update(ref, emulate(x, w, fmt))
+
+
+class LayerGraph:
+    """:func:`layer_sums` for one layer shape captured once as a CUDA graph over static input and
+    output buffers. A layer then costs the host two input copies, one replay and one copy of the sums,
+    instead of the ~15 library calls and ~30 tensor operations of an eager pass (about 3 ms of Python
+    per layer, as long as the device work itself)."""
+
+    def __init__(self, fin: int, fout: int, tokens: int, device):
+        device = torch.device(device)
+        g = torch.Generator(device=device)
+        g.manual_seed(fin * 7919 + fout)
+        self.x = torch.randn((tokens, fin), generator=g, device=device).bfloat16()
+        self.w = (torch.randn((fout, fin), generator=g, device=device) * 0.02).bfloat16()
+        self.sums = torch.zeros((len(FORMATS), len(METRIC_FIELDS)), dtype=torch.float64, device=device)
+        current = torch.cuda.current_stream(device)
+        side = torch.cuda.Stream(device)
+        side.wait_stream(current)
+        with torch.cuda.stream(side):  # one eager pass first: allocations and first launches
+            self._body()
+        current.wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._body()
+
+    def _body(self) -> None:
+        self.sums.zero_()
+        layer_sums(self.x, self.w, self.sums)
+
+    def run(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> None:
+        self.x.copy_(x)
+        self.w.copy_(w)
+        self.graph.replay()
+        out.copy_(self.sums)
+
+
+_GRAPHS: dict = {}
+
+
+def layer_graph(fin: int, fout: int, tokens: int, device) -> LayerGraph:
+    key = (torch.device(device).index, fin, fout, tokens)
+    if key not in _GRAPHS:
+        _GRAPHS[key] = LayerGraph(fin, fout, tokens, device)
+    return _GRAPHS[key]
+
+
+def release_graphs() -> None:
+    """Drop the captured layer graphs (before the process group is destroyed, or to free memory)."""
+    _GRAPHS.clear()
+
+
+def run_layers(entries: list, cfg: SweepConfig, device, out_dir: str | None = None,
+               graphs: bool = True) -> torch.Tensor:
+    """Metric sums [len(entries), len(FORMATS), 6] (fp64, on the device) for this rank's layers; with
+    ``graphs`` each layer replays its shape's captured :class:`LayerGraph`, else runs eagerly."""
     sums = torch.zeros((len(entries), len(FORMATS), len(METRIC_FIELDS)), dtype=torch.float64, device=device)
     for row, (index, name, fin, fout) in enumerate(entries):
         record = None if out_dir is None else Path(out_dir) / f"layer_{index:04d}.json"
@@ -165,11 +226,10 @@ def run_layers(entries: list, cfg: SweepConfig, device, out_dir: str | None = No
                 sums[row] = torch.tensor(saved["sums"], dtype=torch.float64, device=device)
                 continue
         x, w = make_layer(index, fin, fout, cfg.tokens, device)
-        ref = reference(x, w)
-        for col, fmt in enumerate(FORMATS):
-            stats = ErrorStats(device)
-            stats.sums = sums[row, col]
-            stats.update(ref, emulate(x, w, fmt))
+        if graphs:
+            layer_graph(fin, fout, cfg.tokens, device).run(x, w, sums[row])
+        else:
+            layer_sums(x, w, sums[row])
         if record is not None:
             record.parent.mkdir(parents=True, exist_ok=True)
             record.write_text(json.dumps({"identity": cfg.identity(), "layer": index, "name": name,
@@ -219,7 +279,7 @@ def results(table: torch.Tensor, cfg: SweepConfig) -> list[dict]:
 
 
 def run_sweep(cfg: SweepConfig | None = None, *, out_dir: str | None = None, costs: dict | None = None,
-              breakdown: dict | None = None) -> tuple[list[dict] | None, float]:
+              breakdown: dict | None = None, graphs: bool = True) -> tuple[list[dict] | None, float]:
     """Run the sweep on this process's rank (torch.distributed initialised for world > 1).
     Returns (records on rank 0 else None, seconds = max over ranks of the device-timed span from the
     first layer's first kernel to the last one's end). ``costs``: per-shape layer costs for the LPT
@@ -240,7 +300,7 @@ def run_sweep(cfg: SweepConfig | None = None, *, out_dir: str | None = None, cos
     end = torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
     start.record()
-    sums = run_layers(mine, cfg, device, out_dir)
+    sums = run_layers(mine, cfg, device, out_dir, graphs)
     end.record()
     host = time.perf_counter() - t0
     end.synchronize()
@@ -285,6 +345,7 @@ def main() -> None:
         if args.json:
             Path(args.json).write_text(json.dumps({"summary": summary, "layers": records}, indent=1))
         print(json.dumps(summary))
+    release_graphs()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
