@@ -216,8 +216,8 @@ def gemm_step(name: str, dev, world: int = 1, rank: int = 0, size: int = 0):
     """(step, macs_whole_job, shape) of one config's step on this rank: quantize all of A and this
     rank's N-column slab of B (against the whole B's amax where the scheme needs it), then the emulated
     GEMM of the slab. At world 1 the slab is all of B. ``size`` (cfg3 only) runs a smaller cube."""
-    from tricast_b200 import as_operand, gemm_triton, quantize_triton, workloads
-    from tricast_b200.shard import column_slab, quantize_shard
+    from tricast_b200 import as_operand, gemm_triton, workloads
+    from tricast_b200.shard import column_slab, quantize_operands
     from tricast_b200.spec import PRESETS, SCHEMES
 
     if name == "cfg2":
@@ -238,8 +238,7 @@ def gemm_step(name: str, dev, world: int = 1, rank: int = 0, size: int = 0):
     a, b = a_cpu.to(dev), b_cpu[s:e].contiguous().to(dev)
 
     def operands(xa=a, xb=b):
-        qa = quantize_triton(xa, scheme_a)
-        qb = quantize_shard(xb, scheme_b)
+        qa, qb = quantize_operands(xa, scheme_a, xb, scheme_b)
         if name == "cfg4":
             return workloads.cfg4_operands(qa, qb)
         return as_operand(qa, compact=True), as_operand(qb, compact=True)

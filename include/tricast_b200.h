@@ -171,6 +171,27 @@ size_t tc_gemm_workspace(const tc_operand *a, const tc_operand *b, const tc_mma_
 int tc_gemm(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec, const float *bias, void *out,
             void *workspace, size_t workspace_bytes, tc_stream stream);
 
+/* Pre-encoded B operands (weights). TriCast keeps a weight operand's packed K-major copy between
+ * calls (src/tricast/mma/operand.py:66-75, nn/linear.py:216-224); these keep the fast path's own
+ * encoding of B instead, so repeated GEMMs against one weight skip re-encoding it.
+ * tc_encode_b_bytes: bytes of B's encoding for GEMMs of A operands like a (same format and scale
+ * layout, and a row count on the same side of 16: more than 16 rows take the tiled kernels, at most
+ * 16 the small-M ones) under spec; 0 when that path takes no pre-encoded B (the tiled GDFS-FP4 path
+ * and the small-M CoFDA path take one). a's values are not read.
+ * tc_encode_b: writes it into enc (device memory the caller owns, at least that many bytes); B's
+ * values and scales are read, asynchronously on stream. A B the fast path cannot take is recorded in
+ * the encoding and sends every GEMM on it to the exact kernel, as tc_gemm does.
+ * tc_gemm_encoded: tc_gemm with B given by its encoding (b still describes B: shape, format, scales
+ * for the exact kernel); workspace as tc_gemm_workspace(a, b, spec). The encoding must come from
+ * tc_encode_b for this b, spec and an A like a; an encoding of another size is rejected with
+ * TC_INVALID_ARGUMENT. */
+size_t tc_encode_b_bytes(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec);
+int tc_encode_b(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec, void *enc, size_t enc_bytes,
+                tc_stream stream);
+int tc_gemm_encoded(const tc_operand *a, const tc_operand *b, const void *b_enc, size_t b_enc_bytes,
+                    const tc_mma_spec *spec, const float *bias, void *out, void *workspace, size_t workspace_bytes,
+                    tc_stream stream);
+
 /* tc_gemm for callers that cannot allocate device memory. No counterpart in TriCast: this entry point
  * exists for hosts that reach the library through a bare C FFI without a CUDA allocator of their own,
  * or that reserve all device memory up front, and so cannot hand tc_gemm a workspace. Same

@@ -69,6 +69,11 @@ EXPORTS = {
     "tc_gemm_workspace": (C.c_size_t, [C.POINTER(TcOperand), C.POINTER(TcOperand), C.POINTER(TcMmaSpec)]),
     "tc_gemm": (C.c_int, [C.POINTER(TcOperand), C.POINTER(TcOperand), C.POINTER(TcMmaSpec), C.c_void_p, C.c_void_p,
                           C.c_void_p, C.c_size_t, C.c_void_p]),
+    "tc_encode_b_bytes": (C.c_size_t, [C.POINTER(TcOperand), C.POINTER(TcOperand), C.POINTER(TcMmaSpec)]),
+    "tc_encode_b": (C.c_int, [C.POINTER(TcOperand), C.POINTER(TcOperand), C.POINTER(TcMmaSpec), C.c_void_p, C.c_size_t,
+                              C.c_void_p]),
+    "tc_gemm_encoded": (C.c_int, [C.POINTER(TcOperand), C.POINTER(TcOperand), C.c_void_p, C.c_size_t,
+                                  C.POINTER(TcMmaSpec), C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "tc_gemm_noalloc": (C.c_int, [C.POINTER(TcOperand), C.POINTER(TcOperand), C.POINTER(TcMmaSpec), C.c_void_p,
                                   C.c_void_p, C.c_void_p]),
     "tc_any_nonfinite": (C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_void_p, C.c_void_p]),

@@ -228,6 +228,7 @@ struct GemmArgs {
   const uint32_t *as, *bs;        // scale words (exact path)
   const int32_t *amul, *bmul;     // multipliers [ntiles * ng][rows_pad]
   const int2 *atw, *btw;          // tile words [ntiles][rows_pad]
+  const int4 *atc, *btc;          // the tensor-core kernel's tile words [ntiles][rows_pad] (tile_words_kernel)
   int64_t a_rows_pad, b_rows_pad;
   int64_t M, N, ntiles;
   int F, shift0;       // shift0 = F - 2 - srad (srad = radix of the combined scale)

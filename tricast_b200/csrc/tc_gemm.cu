@@ -163,6 +163,30 @@ extern "C" int tc_gemm(const tc_operand *a, const tc_operand *b, const tc_mma_sp
   return TC_OK;
 }
 
+extern "C" size_t tc_encode_b_bytes(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec) {
+  GemmDesc g;
+  if (build_desc(a, b, spec, nullptr, (void *)1, g)) return 0;
+  return encoded_b_bytes(g);
+}
+
+extern "C" int tc_encode_b(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec, void *enc,
+                           size_t enc_bytes, tc_stream stream) {
+  GemmDesc g;
+  int st = build_desc(a, b, spec, nullptr, (void *)1, g);
+  if (st) return st;
+  return encode_b(g, enc, enc_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int tc_gemm_encoded(const tc_operand *a, const tc_operand *b, const void *b_enc, size_t b_enc_bytes,
+                               const tc_mma_spec *spec, const float *bias, void *out, void *workspace,
+                               size_t workspace_bytes, tc_stream stream) {
+  GemmDesc g;
+  int st = build_desc(a, b, spec, bias, out, g);
+  if (st) return st;
+  if (g.M == 0 || g.N == 0) return TC_OK;
+  return launch_fast_encoded(g, b_enc, b_enc_bytes, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
 namespace tc {
 uint64_t gemv_exact_fallbacks();
 }

@@ -62,7 +62,16 @@ int build_desc(const tc_operand *a, const tc_operand *b, const tc_mma_spec *spec
 
 // Fast kernels (tc_gemm_fast.cu): return TC_UNSUPPORTED when the case is not theirs.
 size_t fast_workspace(const GemmDesc &g);
-int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
+int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s,
+                const void *benc = nullptr);
+
+// Pre-encoded B operands (tc_encode_b): bytes of B's encoding for this operand pair and spec (0: the
+// pair's fast path takes none), the encoder, and the GEMM on an encoded B. The tiled GDFS-FP4 path
+// (A of more than 16 rows) and the small-M CoFDA path (at most 16) take one.
+size_t encoded_b_bytes(const GemmDesc &g);
+int encode_b(const GemmDesc &g, void *enc, size_t enc_bytes, cudaStream_t s);
+int launch_fast_encoded(const GemmDesc &g, const void *benc, size_t enc_bytes, void *workspace,
+                        size_t workspace_bytes, cudaStream_t s);
 
 // The exact generic kernel; with only_if_flag it runs only when *only_if_flag != 0.
 void launch_generic(const GemmDesc &g, const int32_t *only_if_flag, cudaStream_t s);

@@ -371,7 +371,28 @@ static CofdaPlan plan_cofda(const GemmDesc &g) {
 
 bool cofda_gemv_eligible(const GemmDesc &g);
 size_t cofda_gemv_workspace(const GemmDesc &g, bool wide);
-int launch_cofda_gemv(const GemmDesc &g, bool wide, void *workspace, size_t workspace_bytes, cudaStream_t s);
+int launch_cofda_gemv(const GemmDesc &g, bool wide, void *workspace, size_t workspace_bytes, cudaStream_t s,
+                      const void *benc = nullptr);
+size_t cofda_gemv_b_bytes(const GemmDesc &g, bool wide);
+int encode_cofda_gemv_b(const GemmDesc &g, bool wide, void *enc, cudaStream_t s);
+
+// Pre-encoded B: the small-M path only (decode shapes, where decoding B is most of the work).
+size_t cofda_encoded_b_bytes(const GemmDesc &g) {
+  const CofdaPlan p = plan_cofda(g);
+  if (!p.ok || !cofda_gemv_eligible(g)) return 0;
+  return cofda_gemv_b_bytes(g, p.wide);
+}
+
+int cofda_encode_b(const GemmDesc &g, void *enc, cudaStream_t s) {
+  const CofdaPlan p = plan_cofda(g);
+  return encode_cofda_gemv_b(g, p.wide, enc, s);
+}
+
+int launch_cofda_encoded(const GemmDesc &g, const void *benc, void *workspace, size_t workspace_bytes,
+                         cudaStream_t s) {
+  const CofdaPlan p = plan_cofda(g);
+  return launch_cofda_gemv(g, p.wide, workspace, workspace_bytes, s, benc);
+}
 
 size_t cofda_workspace(const GemmDesc &g) {
   CofdaPlan p = plan_cofda(g);

@@ -155,9 +155,24 @@ __global__ void __launch_bounds__(256) encode_fp4_kernel(EncodeArgs e) {
 // +-(ms << (es - minE)) (0 for an all-zero group). tw = {minE, L}: {kBig, kNone} when every group is
 // zero, L = kBig when the exponent spread exceeds 11 (the multiplier bound), which forces the exact
 // path for every output that uses the row.
+//
+// tcw (optional, for the tensor-core kernel): the tile words re-expressed so that the per-output tile
+// step is a handful of adds and compares. For an output (row of A with {ea, la}, column of B with
+// {eb, lb}) the single-pass conditions and the fp64 power are sums of a row part and a column part:
+//   lo   = la + lb - (F - 23) + 127         row: la - (F - 23) + 127   column: lb
+//   hi   = ea + eb + F - srad2 + 127        (stored as the span hi - lo, a row part plus a column part)
+//   d    = (ea - la) + (eb - lb) - (srad2 - F)   row: ea - la - (srad2 - F)   column: eb - lb
+//   p2   = 2**(ea + eb - srad2), its fp64 high word ((ea + eb - srad2 + 1023) << 20):
+//          row: (ea' - srad2 + 1023) << 20   column: eb' << 20, with ea', eb' clamped to [-500, 500]
+// so words are {lo part, span part, d part, p2 part}. The biased exponent be of the running value
+// passes lo <= be <= hi iff (unsigned)(be - lo) <= (unsigned)(hi - lo) whenever d >= 0 (then
+// hi - lo = d + F - 23 >= 0), which the step also requires. Scale exponents are within +-400 except
+// for the all-zero sentinel, whose acc is 0, so the clamp changes no result and keeps the power a
+// normal double.
 __global__ void __launch_bounds__(256) tile_words_kernel(const uint32_t *__restrict__ sw, int64_t rows_pad,
                                                          int64_t ntiles, int ng, int32_t *__restrict__ mult,
-                                                         int2 *__restrict__ tw) {
+                                                         int2 *__restrict__ tw, int4 *__restrict__ tcw, int side,
+                                                         int F, int srad2) {
   const int64_t total = ntiles * rows_pad;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
@@ -182,7 +197,14 @@ __global__ void __launch_bounds__(256) tile_words_kernel(const uint32_t *__restr
       }
       mult[gi] = m;
     }
-    tw[idx] = make_int2(min_e, wide ? kBig : max_l);
+    const int ea = min_e, la = wide ? kBig : max_l;
+    tw[idx] = make_int2(ea, la);
+    if (tcw) {
+      const int ec = min(max(ea, -500), 500);
+      tcw[idx] = side == 0 ? make_int4(la - (F - 23) + 127, (ea + F - srad2 + 127) - (la - (F - 23) + 127),
+                                       ea - la - (srad2 - F), (ec - srad2 + 1023) << 20)
+                           : make_int4(la, ea - la, ea - la, ec << 20);
+    }
   }
 }
 
@@ -426,8 +448,9 @@ struct Fp4Plan {
   bool ok;
   int ng;
   int64_t ntiles, a_pad, b_pad;
-  // per side (A then B): codes, masks, scale words, multipliers, tile words
-  size_t off[10], bytes[10], flag_off, total;
+  // per side (A then B): codes, masks, scale words, multipliers, tile words; then the tensor-core
+  // kernel's tile words of A and of B
+  size_t off[12], bytes[12], flag_off, total;
 };
 
 static bool is_e2m1(const Fmt &f) { return f.kind == 0 && f.mbits == 1 && f.emin == 0 && f.emax == 2 && f.is_signed; }
@@ -450,10 +473,11 @@ static Fp4Plan plan_fp4(const GemmDesc &g) {
   p.a_pad = (g.M + 127) / 128 * 128;  // whole 128-row tiles for the tensor-core kernel (64 for the DP4A one)
   p.b_pad = (g.N + fp4::kTileRows - 1) / fp4::kTileRows * fp4::kTileRows;
   int64_t ga = p.ntiles * p.ng * p.a_pad, gb = p.ntiles * p.ng * p.b_pad;
-  size_t sizes[10] = {(size_t)ga * 16, (size_t)ga * 16, (size_t)ga * 4, (size_t)ga * 4, (size_t)(p.ntiles * p.a_pad) * 8,
-                      (size_t)gb * 16, (size_t)gb * 16, (size_t)gb * 4, (size_t)gb * 4, (size_t)(p.ntiles * p.b_pad) * 8};
+  size_t sizes[12] = {(size_t)ga * 16, (size_t)ga * 16, (size_t)ga * 4, (size_t)ga * 4, (size_t)(p.ntiles * p.a_pad) * 8,
+                      (size_t)gb * 16, (size_t)gb * 16, (size_t)gb * 4, (size_t)gb * 4, (size_t)(p.ntiles * p.b_pad) * 8,
+                      (size_t)(p.ntiles * p.a_pad) * 16, (size_t)(p.ntiles * p.b_pad) * 16};
   size_t off = 0;
-  for (int i = 0; i < 10; ++i) {
+  for (int i = 0; i < 12; ++i) {
     p.off[i] = off;
     p.bytes[i] = sizes[i];
     off += (sizes[i] + 255) & ~(size_t)255;
@@ -502,7 +526,108 @@ static int launch_fp4_gemm(const fp4::GemmArgs &args, int64_t M, int64_t N, cuda
   return args.rne ? launch_fp4_gemm_r<NG, true>(args, M, N, s) : launch_fp4_gemm_r<NG, false>(args, M, N, s);
 }
 
-int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s) {
+// One operand's GDFS-FP4 records: the encoder (codes, class masks, scale words) and the tile words
+// (multipliers, tile bounds, the tensor-core kernel's tile words), into the given arrays.
+static void encode_fp4_side(const GemmDesc &g, const Fp4Plan &p, int side, char *q, char *m, char *sw, char *mult,
+                            char *tw, char *tcw, int32_t *flag, int srad2, cudaStream_t s) {
+  const OpDesc &o = side ? g.b : g.a;
+  fp4::EncodeArgs e;
+  e.v = o.v;
+  e.dt = o.dt;
+  e.rows = o.rows;
+  e.K = o.K;
+  e.rows_pad = side ? p.b_pad : p.a_pad;
+  e.ntiles = p.ntiles;
+  e.ng = p.ng;
+  e.scale = o.skind == SK_K ? o.scale : nullptr;
+  e.nkd = o.nkd;
+  e.kd = o.kd;
+  e.sf = o.sf;
+  e.field0 = o.field0;
+  e.q = reinterpret_cast<uint4 *>(q);
+  e.m = reinterpret_cast<uint4 *>(m);
+  e.s = reinterpret_cast<uint32_t *>(sw);
+  e.flag = flag;
+  e.side = side;
+  const int esz = o.dt == TC_F32 ? 4 : 2;
+  e.vec = ((uintptr_t)o.v % 16 == 0) && ((o.K * esz) % 16 == 0);
+  const int64_t work = p.ntiles * p.ng * e.rows_pad;
+  const int64_t blocks = std::min<int64_t>((work + 255) / 256, (int64_t)sm_count() * 16);
+  fp4::encode_fp4_kernel<<<(unsigned)blocks, 256, 0, s>>>(e);
+  count_launch();
+  const int64_t twork = p.ntiles * e.rows_pad;
+  const int64_t tblocks = std::min<int64_t>((twork + 255) / 256, (int64_t)sm_count() * 16);
+  fp4::tile_words_kernel<<<(unsigned)tblocks, 256, 0, s>>>(e.s, e.rows_pad, p.ntiles, p.ng,
+                                                           reinterpret_cast<int32_t *>(mult), reinterpret_cast<int2 *>(tw),
+                                                           reinterpret_cast<int4 *>(tcw), side, g.F, srad2);
+  count_launch();
+}
+
+// A pre-encoded B of the tiled GDFS-FP4 path: B's records and tile words (the plan's B arrays and the
+// tensor-core tile words of B), each 256-byte aligned, then a flag word set when B cannot be encoded.
+struct Fp4BLayout {
+  size_t off[6], flag_off, total;
+};
+
+static Fp4BLayout fp4_b_layout(const Fp4Plan &p) {
+  Fp4BLayout l;
+  const int idx[6] = {5, 6, 7, 8, 9, 11};
+  size_t off = 0;
+  for (int i = 0; i < 6; ++i) {
+    l.off[i] = off;
+    off += (p.bytes[idx[i]] + 255) & ~(size_t)255;
+  }
+  l.flag_off = off;
+  l.total = off + 256;
+  return l;
+}
+
+size_t cofda_encoded_b_bytes(const GemmDesc &g);
+int cofda_encode_b(const GemmDesc &g, void *enc, cudaStream_t s);
+int launch_cofda_encoded(const GemmDesc &g, const void *benc, void *workspace, size_t workspace_bytes,
+                         cudaStream_t s);
+
+static bool fp4_tiled_encodable(const GemmDesc &g, const Fp4Plan &p) {
+  return p.ok && g.M > kGemvMaxM && p.ntiles * fp4::kTileRows <= ((int64_t)1 << 40);
+}
+
+size_t encoded_b_bytes(const GemmDesc &g) {
+  const Fp4Plan p = plan_fp4(g);
+  if (p.ok) return fp4_tiled_encodable(g, p) ? fp4_b_layout(p).total : 0;
+  if (int_workspace(g)) return 0;  // integer operands: encoded per call
+  return cofda_encoded_b_bytes(g);
+}
+
+int encode_b(const GemmDesc &g, void *enc, size_t enc_bytes, cudaStream_t s) {
+  const size_t need = encoded_b_bytes(g);
+  if (!need) return set_error("tc_encode_b: this operand pair has no path that takes a pre-encoded B"), TC_UNSUPPORTED;
+  if (!enc || enc_bytes < need) return set_error("tc_encode_b: buffer too small"), TC_INVALID_ARGUMENT;
+  const Fp4Plan p = plan_fp4(g);
+  if (!p.ok) return cofda_encode_b(g, enc, s);
+  const Fp4BLayout l = fp4_b_layout(p);
+  char *e = static_cast<char *>(enc);
+  int32_t *flag = reinterpret_cast<int32_t *>(e + l.flag_off);
+  cudaMemsetAsync(flag, 0, sizeof(int32_t), s);
+  const int srad = (g.a.skind == SK_K ? g.a.srad : 0) + (g.b.skind == SK_K ? g.b.srad : 0);
+  encode_fp4_side(g, p, 1, e + l.off[0], e + l.off[1], e + l.off[2], e + l.off[3], e + l.off[4], e + l.off[5], flag,
+                  srad + 2, s);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return set_error(std::string("tc_encode_b: ") + cudaGetErrorString(err)), TC_CUDA_ERROR;
+  return TC_OK;
+}
+
+int launch_fast_encoded(const GemmDesc &g, const void *benc, size_t enc_bytes, void *workspace, size_t workspace_bytes,
+                        cudaStream_t s) {
+  const size_t need = encoded_b_bytes(g);
+  if (!need || enc_bytes != need || !benc)
+    return set_error("tc_gemm_encoded: the encoded B was made for another operand pair, spec or row count"),
+           TC_INVALID_ARGUMENT;
+  const Fp4Plan p = plan_fp4(g);
+  if (!p.ok) return launch_cofda_encoded(g, benc, workspace, workspace_bytes, s);
+  return launch_fast(g, workspace, workspace_bytes, s, benc);
+}
+
+int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s, const void *benc) {
   Fp4Plan p = plan_fp4(g);
   if (!p.ok) {
     int st = launch_int(g, workspace, workspace_bytes, s);
@@ -517,39 +642,19 @@ int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
   char *ws = static_cast<char *>(workspace);
   int32_t *flag = reinterpret_cast<int32_t *>(ws + p.flag_off);
   cudaMemsetAsync(flag, 0, 2 * sizeof(int32_t), s);
-  for (int side = 0; side < 2; ++side) {
-    const OpDesc &o = side ? g.b : g.a;
-    fp4::EncodeArgs e;
-    e.v = o.v;
-    e.dt = o.dt;
-    e.rows = o.rows;
-    e.K = o.K;
-    e.rows_pad = side ? p.b_pad : p.a_pad;
-    e.ntiles = p.ntiles;
-    e.ng = p.ng;
-    e.scale = o.skind == SK_K ? o.scale : nullptr;
-    e.nkd = o.nkd;
-    e.kd = o.kd;
-    e.sf = o.sf;
-    e.field0 = o.field0;
-    e.q = reinterpret_cast<uint4 *>(ws + p.off[side * 5 + 0]);
-    e.m = reinterpret_cast<uint4 *>(ws + p.off[side * 5 + 1]);
-    e.s = reinterpret_cast<uint32_t *>(ws + p.off[side * 5 + 2]);
-    e.flag = flag;
-    e.side = side;
-    const int esz = o.dt == TC_F32 ? 4 : 2;
-    e.vec = ((uintptr_t)o.v % 16 == 0) && ((o.K * esz) % 16 == 0);
-    int64_t work = p.ntiles * p.ng * e.rows_pad;
-    int64_t blocks = (work + 255) / 256;
-    if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
-    fp4::encode_fp4_kernel<<<(unsigned)blocks, 256, 0, s>>>(e);
-    count_launch();
-    const int64_t twork = p.ntiles * e.rows_pad;
-    const int64_t tblocks = std::min<int64_t>((twork + 255) / 256, (int64_t)sm_count() * 16);
-    fp4::tile_words_kernel<<<(unsigned)tblocks, 256, 0, s>>>(e.s, e.rows_pad, p.ntiles, p.ng,
-                                                             reinterpret_cast<int32_t *>(ws + p.off[side * 5 + 3]),
-                                                             reinterpret_cast<int2 *>(ws + p.off[side * 5 + 4]));
-    count_launch();
+  if (benc)  // a B the encoder could not take gates this product like one rejected now
+    cudaMemcpyAsync(flag, static_cast<const char *>(benc) + fp4_b_layout(p).flag_off, sizeof(int32_t),
+                    cudaMemcpyDeviceToDevice, s);
+  const int srad = (g.a.skind == SK_K ? g.a.srad : 0) + (g.b.skind == SK_K ? g.b.srad : 0);
+  const int srad2 = srad + 2;
+  // A is encoded on every call; B too unless the caller passed it pre-encoded (tc_encode_b).
+  for (int side = 0; side < (benc ? 1 : 2); ++side)
+    encode_fp4_side(g, p, side, ws + p.off[side * 5 + 0], ws + p.off[side * 5 + 1], ws + p.off[side * 5 + 2],
+                    ws + p.off[side * 5 + 3], ws + p.off[side * 5 + 4], ws + p.off[10 + side], flag, srad2, s);
+  const char *bsrc[6] = {ws + p.off[5], ws + p.off[6], ws + p.off[7], ws + p.off[8], ws + p.off[9], ws + p.off[11]};
+  if (benc) {
+    const Fp4BLayout l = fp4_b_layout(p);
+    for (int i = 0; i < 6; ++i) bsrc[i] = static_cast<const char *>(benc) + l.off[i];
   }
   fp4::GemmArgs a;
   a.aq = reinterpret_cast<const uint4 *>(ws + p.off[0]);
@@ -557,18 +662,19 @@ int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
   a.as = reinterpret_cast<const uint32_t *>(ws + p.off[2]);
   a.amul = reinterpret_cast<const int32_t *>(ws + p.off[3]);
   a.atw = reinterpret_cast<const int2 *>(ws + p.off[4]);
-  a.bq = reinterpret_cast<const uint4 *>(ws + p.off[5]);
-  a.bm = reinterpret_cast<const uint4 *>(ws + p.off[6]);
-  a.bs = reinterpret_cast<const uint32_t *>(ws + p.off[7]);
-  a.bmul = reinterpret_cast<const int32_t *>(ws + p.off[8]);
-  a.btw = reinterpret_cast<const int2 *>(ws + p.off[9]);
+  a.bq = reinterpret_cast<const uint4 *>(bsrc[0]);
+  a.bm = reinterpret_cast<const uint4 *>(bsrc[1]);
+  a.bs = reinterpret_cast<const uint32_t *>(bsrc[2]);
+  a.bmul = reinterpret_cast<const int32_t *>(bsrc[3]);
+  a.btw = reinterpret_cast<const int2 *>(bsrc[4]);
+  a.atc = reinterpret_cast<const int4 *>(ws + p.off[10]);
+  a.btc = reinterpret_cast<const int4 *>(bsrc[5]);
   a.a_rows_pad = p.a_pad;
   a.b_rows_pad = p.b_pad;
   a.M = g.M;
   a.N = g.N;
   a.ntiles = p.ntiles;
   a.F = g.F;
-  int srad = (g.a.skind == SK_K ? g.a.srad : 0) + (g.b.skind == SK_K ? g.b.srad : 0);
   a.shift0 = g.F - 2 - srad;
   a.srad2 = srad + 2;
   a.pexp = 1023 - (srad + 2);

@@ -49,8 +49,8 @@ struct Stage {
   uint4 bq[NG][kN];
   int32_t amul[NG][kM];
   int32_t bmul[NG][kN];
-  int2 atw[kM];
-  int2 btw[kN];
+  int4 atc[kM];      // row parts of the tile-step bounds and power (tile_words_kernel)
+  int4 btc[kN];      // column parts
 };
 
 // The exact two-pass tile step for one output whose tile failed the single-pass bounds (rare). Called
@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdfs_fp4_tc_kernel(const __grid_c
   if (warp == kEpiWarps) {
     if (lane == 0) {
       // Producer and MMA issuer (one thread).
-      constexpr uint32_t kStageBytes = NG * (kM * 16 + kN * 16 + kM * 4 + kN * 4) + kM * 8 + kN * 8;
+      constexpr uint32_t kStageBytes = NG * (kM * 16 + kN * 16 + kM * 4 + kN * 4) + kM * 16 + kN * 16;
       bool ok = true;
       int64_t issued = 0, waited_full = 0, last = -1;
       auto issue = [&](int64_t t) {
@@ -149,8 +149,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdfs_fp4_tc_kernel(const __grid_c
           bulk_g2s(st.amul[gg], g.amul + ga, kM * 4, bar);
           bulk_g2s(st.bmul[gg], g.bmul + gb, kN * 4, bar);
         }
-        bulk_g2s(st.atw, g.atw + t * g.a_rows_pad + m0, kM * 8, bar);
-        bulk_g2s(st.btw, g.btw + t * g.b_rows_pad + n0, kN * 8, bar);
+        bulk_g2s(st.atc, g.atc + t * g.a_rows_pad + m0, kM * 16, bar);
+        bulk_g2s(st.btc, g.btc + t * g.b_rows_pad + n0, kN * 16, bar);
         issued = t + 1;
       };
       for (int64_t t = 0; t < kStages && t < g.ntiles; ++t) issue(t);
@@ -202,44 +202,53 @@ __global__ void __launch_bounds__(kThreads, 1) gdfs_fp4_tc_kernel(const __grid_c
       }
       tc5::fence_after_sync();
       const Stage<NG> &st = stages[s];
-      // Tile step (the tiled kernel's bounds, per output): single pass or the exact fallback. kChunk
-      // columns at a time, so that the int64 sums fit the 96 registers a thread has (17 warps: five
-      // share one sub-partition's register file) without spilling.
-      const int2 wa = st.atw[row];
+      // Tile step per output (the tiled kernel's single-pass bounds): the int64 tile sum of the group
+      // sums times their multipliers, then c + sum * 2**(ea + eb - srad2) in fp64 (exact under the
+      // bounds) and one rounding to fp32. The bounds and the power are a row part (this thread's) plus
+      // a column part (tile_words_kernel). TMEM is read kChunk columns x NG groups at a time with one
+      // wait per chunk. (17 warps leave 96 registers a thread: five warps share one sub-partition's
+      // register file, so the chunk's loads are not double-buffered.)
+      const int4 rw = st.atc[row];
+      const int nd = -rw.z;  // d = rw.z + cw.z >= 0  <=>  cw.z >= -rw.z
+      int ma[NG];
+#pragma unroll
+      for (int gg = 0; gg < NG; ++gg) ma[gg] = st.amul[gg][row];
+      const uint32_t buf = lane_addr + (uint32_t)(b * NG * kN);
       uint32_t unsafe = 0;
 #pragma unroll
       for (int h = 0; h < kCols / kChunk; ++h) {
-        int64_t acc[kChunk];
+        uint32_t dh[NG * kChunk];
 #pragma unroll
-        for (int j = 0; j < kChunk; ++j) acc[j] = 0;
+        for (int gg = 0; gg < NG; ++gg)
+          tc5::tmem_ld4_nowait(buf + (uint32_t)(gg * kN + h * kChunk), *reinterpret_cast<uint32_t(*)[4]>(&dh[gg * kChunk]));
+        tc5::tmem_wait_ld<NG * kChunk>(dh);
+        int4 bm[NG];
 #pragma unroll
-        for (int gg = 0; gg < NG; ++gg) {
-          uint32_t d[kChunk];
-          tc5::tmem_ld<kChunk>(lane_addr + (uint32_t)((b * NG + gg) * kN + h * kChunk), d);
-          const int ma = st.amul[gg][row];
-#pragma unroll
-          for (int j = 0; j < kChunk; ++j) acc[j] += (int64_t)(int)d[j] * (int64_t)(ma * st.bmul[gg][col0 + h * kChunk + j]);
-        }
+        for (int gg = 0; gg < NG; ++gg) bm[gg] = *reinterpret_cast<const int4 *>(&st.bmul[gg][col0 + h * kChunk]);
 #pragma unroll
         for (int jj = 0; jj < kChunk; ++jj) {
           const int j = h * kChunk + jj;
-          const int2 wb = st.btw[col0 + j];
+          int64_t acc = 0;
+#pragma unroll
+          for (int gg = 0; gg < NG; ++gg) {
+            const int mb = jj == 0 ? bm[gg].x : jj == 1 ? bm[gg].y : jj == 2 ? bm[gg].z : bm[gg].w;
+            acc += (int64_t)(int)dh[gg * kChunk + jj] * (int64_t)(ma[gg] * mb);
+          }
+          const int4 cw = st.btc[col0 + j];
           const uint32_t cb = f2u(c[j]) & 0x7FFFFFFFu;
-          const int be = (int)(cb >> 23);
-          const int lo = max(wa.y + wb.y - (g.F - 23) + 127, 1);
-          const int hi = wa.x + wb.x + g.F - g.srad2 + 127;
-          const bool safe = (wa.x - wa.y) + (wb.x - wb.y) >= g.srad2 - g.F &&
-                            ((cb == 0) | (cb >= kInf) | ((be >= lo) & (be <= hi)));
-          // c + acc * 2**(min es_a + min es_b - srad - 2), exact in fp64 (the clamp only matters for an
-          // all-zero row or column, whose acc is 0). Computed for every output and kept only where the
-          // bounds hold (no branch: the unsafe outputs are rare and redone below).
-          const int e2 = min(max(wa.x + wb.x - g.srad2, -1000), 1000);
-          const double p2 = __hiloint2double((e2 + 1023) << 20, 0);
-          const double v = __fma_rn((double)acc[jj], p2, (double)c[j]);
-          float r = (RNE && fabs(v) >= 0x1p-126) ? __double2float_rn(v) : __double2float_rz(v);
-          r = fabs(v) >= 0x1p128 ? __int_as_float((int)((f2u(r) & 0x80000000u) | kInf)) : r;
-          c[j] = (safe && cb < kInf) ? r : c[j];  // an Inf / NaN running value is sticky
-          unsafe |= safe ? 0u : 1u << j;
+          const int be = max((int)(cb >> 23), 1);  // a subnormal c has the lsb and exponent of field 1
+          // The terms' quanta allow one pass (d >= 0), and c keeps its bits at the tile's radix (its
+          // lsb and magnitude within the window) or is zero.
+          const bool keeps = ((uint32_t)(be - rw.x - cw.x) <= (uint32_t)(rw.y + cw.y)) | (cb == 0u);
+          const bool safe = (cw.z >= nd) & keeps;
+          const double p2 = __hiloint2double(rw.w + cw.w, 0);
+          const double v = __fma_rn((double)acc, p2, (double)c[j]);
+          const float r = (RNE && fabs(v) >= 0x1p-126) ? __double2float_rn(v) : __double2float_rz(v);
+          // |v| >= 2**128 overflows the fixed-point normalisation: the exact step decides.
+          const bool fits = fabs(v) < 0x1p128;
+          const bool take = safe & fits & (cb < kInf);  // an Inf / NaN running value is sticky
+          c[j] = take ? r : c[j];
+          unsafe |= (!take & (cb < kInf)) ? 1u << j : 0u;
         }
       }
       // Exact two-pass tile step for the outputs that failed the bounds (rare): each round, every lane

@@ -53,6 +53,8 @@ struct Args {
   int sa_kd, sb_kd;
   GemmDesc g;                // epilogue
   int32_t *flag;             // nonzero: the fast path cannot take the operands
+  const T *bval_enc;         // pre-encoded B (tc_encode_b): values [N][Kp] as prep_a_kernel writes them
+  const int16_t *bexp_enc;   // and labels
 };
 
 struct PrepArgs {
@@ -180,7 +182,9 @@ __device__ __forceinline__ int group_max(int v) {
   return v;
 }
 
-template <int CS, int LG, class T>
+// BENC: B arrives pre-encoded (values and labels [N][Kp], prep_a_kernel's layout) and is staged with
+// asynchronous copies one step ahead, like A, instead of being loaded and decoded here.
+template <int CS, int LG, class T, bool BENC>
 __global__ void __launch_bounds__(kThreads) cofda_gemv_kernel(Args<T> p) {
   constexpr int PL = CS / LG;  // products per lane per chunk
   if (*p.flag) return;         // A could not be decoded: the generic kernel takes over
@@ -239,13 +243,30 @@ __global__ void __launch_bounds__(kThreads) cofda_gemv_kernel(Args<T> p) {
     }
     cp_async_commit();
   };
+  // B's values and labels of one step into slot step & 1 (pre-encoded B only).
+  auto copy_b = [&](int64_t step) {
+    const int slot = (int)(step & 1);
+    const int vpr = p.KC * (int)sizeof(T) / 16, epr = p.KC * 2 / 16;
+    for (int i = threadIdx.x; i < p.cols * (vpr + epr); i += kThreads) {
+      const int c = i / (vpr + epr), r = i % (vpr + epr);
+      if (n0 + c >= p.N) continue;  // columns past N are scanned by idle slots only
+      if (r < vpr)
+        cp_async16(reinterpret_cast<char *>(bval + ((size_t)slot * p.cols + c) * stride) + 16 * r,
+                   reinterpret_cast<const char *>(p.bval_enc + (n0 + c) * p.Kp + step * p.KC) + 16 * r);
+      else
+        cp_async16(reinterpret_cast<char *>(bexp + ((size_t)slot * p.cols + c) * stride) + 16 * (r - vpr),
+                   reinterpret_cast<const char *>(p.bexp_enc + (n0 + c) * p.Kp + step * p.KC) + 16 * (r - vpr));
+    }
+    cp_async_commit();
+  };
   copy_a(0);
-  fetch(0);
+  if constexpr (BENC) copy_b(0);
+  else fetch(0);
   for (int64_t step = 0; step < nsteps; ++step) {
     const int buf = (int)(step & 1);
     T *sv = bval + (size_t)buf * p.cols * stride;
     int16_t *se = bexp + (size_t)buf * p.cols * stride;
-    {
+    if constexpr (!BENC) {
       const int64_t k = step * p.KC + lk;
       float x[kPerThread];
       if (ln < p.N && p.bvec && k + kPerThread <= p.K) {
@@ -301,11 +322,15 @@ __global__ void __launch_bounds__(kThreads) cofda_gemv_kernel(Args<T> p) {
         *reinterpret_cast<uint4 *>(se + (size_t)lcol * stride + lk + 8) = *reinterpret_cast<const uint4 *>(labs + 8);
       }
     }
-    if (step + 1 < nsteps) fetch(step + 1);  // in flight while this step is scanned
-    cp_async_wait_all();                       // this step's A (issued one step earlier)
+    if constexpr (!BENC)
+      if (step + 1 < nsteps) fetch(step + 1);  // in flight while this step is scanned
+    cp_async_wait_all();                       // this step's A (and pre-encoded B), issued one step earlier
     __syncthreads();
-    // The other A slot was last read by the previous step's scan, which every thread has finished.
-    if (step + 1 < nsteps) copy_a(step + 1);
+    // The other slots were last read by the previous step's scan, which every thread has finished.
+    if (step + 1 < nsteps) {
+      copy_a(step + 1);
+      if constexpr (BENC) copy_b(step + 1);
+    }
     const T *bv_col = sv + (size_t)scol_c * stride + j * PL;
     const int16_t *be_col = se + (size_t)scol_c * stride + j * PL;
     const T *av_row = aval_s + ((size_t)(step & 1) * M + sm) * stride + j * PL;
@@ -380,16 +405,75 @@ bool cofda_gemv_eligible(const GemmDesc &g) {
 
 size_t cofda_gemv_workspace(const GemmDesc &g, bool wide) { return plan_cofda_gemv(g, wide).total; }
 
-template <int CS, int LG, class T>
-static int launch_cofda_gemv_t(const cgemv::Args<T> &a, cudaStream_t s) {
+// A pre-encoded B of the small-M path: B's elements decoded as A's are (values with the folded
+// power-of-two product scales, and labels), [N][Kp] each, then a flag word set when B cannot be taken.
+struct CofdaGemvBLayout {
+  int64_t Kp;
+  size_t off_val, off_exp, off_flag, total;
+};
+
+static CofdaGemvBLayout cofda_gemv_b_layout(const GemmDesc &g, bool wide) {
+  CofdaGemvBLayout l;
+  l.Kp = (g.K + cgemv::kMaxKC - 1) / cgemv::kMaxKC * cgemv::kMaxKC;
+  const size_t n = (size_t)g.N * l.Kp;
+  auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
+  l.off_val = 0;
+  l.off_exp = up(n * (wide ? 8 : 4));
+  l.off_flag = l.off_exp + up(n * 2);
+  l.total = l.off_flag + 256;
+  return l;
+}
+
+size_t cofda_gemv_b_bytes(const GemmDesc &g, bool wide) { return cofda_gemv_b_layout(g, wide).total; }
+
+int encode_cofda_gemv_b(const GemmDesc &g, bool wide, void *enc, cudaStream_t s) {
+  const CofdaGemvBLayout l = cofda_gemv_b_layout(g, wide);
+  char *e = static_cast<char *>(enc);
+  int32_t *flag = reinterpret_cast<int32_t *>(e + l.off_flag);
+  cudaMemsetAsync(flag, 0, sizeof(int32_t), s);
+  if (g.N > 0 && l.Kp > 0) {
+    cgemv::PrepArgs pa;
+    std::memset(&pa, 0, sizeof(pa));
+    pa.v = g.b.v;
+    pa.dt = g.b.dt;
+    pa.rows = g.N;
+    pa.K = g.K;
+    pa.Kp = l.Kp;
+    pa.f = g.b.f;
+    pa.scale = (g.apply == AP_PRODUCT && g.b.skind == SK_K) ? g.b.scale : nullptr;
+    pa.nkd = g.b.nkd;
+    pa.kd = g.b.kd;
+    pa.sf = g.b.sf;
+    pa.field0 = g.b.field0;
+    pa.val = e + l.off_val;
+    pa.exp = reinterpret_cast<int16_t *>(e + l.off_exp);
+    pa.flag = flag;
+    const int64_t work = g.N * l.Kp;
+    const int64_t blocks = std::min<int64_t>((work + 255) / 256, (int64_t)sm_count() * 8);
+    if (wide) cgemv::prep_a_kernel<double><<<(unsigned)blocks, 256, 0, s>>>(pa);
+    else cgemv::prep_a_kernel<float><<<(unsigned)blocks, 256, 0, s>>>(pa);
+    count_launch();
+  }
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return set_error(std::string("tc_encode_b: ") + cudaGetErrorString(err)), TC_CUDA_ERROR;
+  return TC_OK;
+}
+
+template <int CS, int LG, class T, bool BENC>
+static int launch_cofda_gemv_b(const cgemv::Args<T> &a, cudaStream_t s) {
   const size_t smem = 2 * (size_t)(a.cols + a.M) * (a.KC + cgemv::kPad) * (sizeof(T) + 2);
-  cudaError_t e = cudaFuncSetAttribute(cgemv::cofda_gemv_kernel<CS, LG, T>,
+  cudaError_t e = cudaFuncSetAttribute(cgemv::cofda_gemv_kernel<CS, LG, T, BENC>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_error(std::string("cofda gemv: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
   const unsigned grid = (unsigned)((a.N + a.cols - 1) / a.cols);
-  cgemv::cofda_gemv_kernel<CS, LG, T><<<grid, cgemv::kThreads, smem, s>>>(a);
+  cgemv::cofda_gemv_kernel<CS, LG, T, BENC><<<grid, cgemv::kThreads, smem, s>>>(a);
   count_launch();
   return TC_OK;
+}
+
+template <int CS, int LG, class T>
+static int launch_cofda_gemv_t(const cgemv::Args<T> &a, cudaStream_t s) {
+  return a.bval_enc ? launch_cofda_gemv_b<CS, LG, T, true>(a, s) : launch_cofda_gemv_b<CS, LG, T, false>(a, s);
 }
 
 template <int LG, class T>
@@ -401,7 +485,7 @@ static int launch_cofda_gemv_cs(const cgemv::Args<T> &a, int CS, cudaStream_t s)
 
 template <class T>
 static int launch_cofda_gemv_typed(const GemmDesc &g, const CofdaGemvPlan &p, char *ws, int32_t *flag,
-                                   cudaStream_t s) {
+                                   const char *benc, cudaStream_t s) {
   if (g.M > 0 && p.Kp > 0) {
     cgemv::PrepArgs e;
     std::memset(&e, 0, sizeof(e));
@@ -456,6 +540,11 @@ static int launch_cofda_gemv_typed(const GemmDesc &g, const CofdaGemvPlan &p, ch
   }
   a.g = g;
   a.flag = flag;
+  if (benc) {
+    const CofdaGemvBLayout l = cofda_gemv_b_layout(g, sizeof(T) == 8);
+    a.bval_enc = reinterpret_cast<const T *>(benc + l.off_val);
+    a.bexp_enc = reinterpret_cast<const int16_t *>(benc + l.off_exp);
+  }
   // Lanes per output: 16 for a single row (twice the CTAs of 8 lanes: 256 for N = 4096), 8 while few
   // rows leave the GPU short of threads, else 4; at least two products per lane and chunk. Columns
   // per CTA: the largest power of two whose M x cols slots fit the CTA.
@@ -472,13 +561,18 @@ static int launch_cofda_gemv_typed(const GemmDesc &g, const CofdaGemvPlan &p, ch
   return LG == 8 ? launch_cofda_gemv_cs<8, T>(a, g.CS, s) : launch_cofda_gemv_cs<4, T>(a, g.CS, s);
 }
 
-int launch_cofda_gemv(const GemmDesc &g, bool wide, void *workspace, size_t workspace_bytes, cudaStream_t s) {
+int launch_cofda_gemv(const GemmDesc &g, bool wide, void *workspace, size_t workspace_bytes, cudaStream_t s,
+                      const void *benc) {
   const CofdaGemvPlan p = plan_cofda_gemv(g, wide);
   if (!workspace || workspace_bytes < p.total) return set_error("tc_gemm: workspace too small"), TC_WORKSPACE_TOO_SMALL;
   char *ws = static_cast<char *>(workspace);
   int32_t *flag = reinterpret_cast<int32_t *>(ws + p.off_flag);
   cudaMemsetAsync(flag, 0, 2 * sizeof(int32_t), s);  // [0] operands rejected, [1] timeout: both gate the generic kernel
-  const int st = wide ? launch_cofda_gemv_typed<double>(g, p, ws, flag, s) : launch_cofda_gemv_typed<float>(g, p, ws, flag, s);
+  const char *b = static_cast<const char *>(benc);
+  if (b)  // a B the encoder rejected gates this product like an A rejected now
+    cudaMemcpyAsync(flag, b + cofda_gemv_b_layout(g, wide).off_flag, sizeof(int32_t), cudaMemcpyDeviceToDevice, s);
+  const int st = wide ? launch_cofda_gemv_typed<double>(g, p, ws, flag, b, s)
+                      : launch_cofda_gemv_typed<float>(g, p, ws, flag, b, s);
   if (st) return st;
   launch_generic(g, flag, s);  // runs only when an operand raised the flag
   cudaError_t e = cudaGetLastError();

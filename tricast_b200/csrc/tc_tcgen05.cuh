@@ -93,6 +93,33 @@ __device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// 4 consecutive 32-bit TMEM columns of this thread's lane (warp-collective), without waiting: the
+// registers hold the values only after tmem_wait_ld on them.
+__device__ __forceinline__ void tmem_ld4_nowait(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(taddr));
+}
+
+// Wait for this thread's outstanding TMEM loads. The N registers they write are passed through the
+// wait as read-write operands, so the compiler cannot move a use of them above it.
+template <int N>
+__device__ __forceinline__ void tmem_wait_ld(uint32_t *r) {
+  static_assert(N == 4 || N == 8 || N == 16, "tmem_wait_ld: 4, 8 or 16 registers");
+  if constexpr (N == 4) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]) :: "memory");
+  } else if constexpr (N == 8) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7])
+                 :: "memory");
+  } else {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :: "memory");
+  }
+}
+
 // N (4, 8 or 16) consecutive 32-bit TMEM columns of this thread's lane (warp-collective), then wait.
 template <int N>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {

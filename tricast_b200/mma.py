@@ -159,9 +159,49 @@ def gemm_triton(a, b, spec, bias: torch.Tensor | None = None) -> torch.Tensor:
     with torch.cuda.device(device):
         ws_bytes = lib.tc_gemm_workspace(pa.desc, pb.desc, ms)
         ws = torch.empty(max(ws_bytes, 1), device=device, dtype=torch.uint8)
-        N.check(lib.tc_gemm(pa.desc, pb.desc, ms, N.ptr(bias_t), N.ptr(out), N.ptr(ws), ws.numel(),
-                            N.stream_of(device)), "tc_gemm")
+        enc = _encoded_b(a, b, spec, apply, pa, pb, ms)
+        if enc is None:
+            N.check(lib.tc_gemm(pa.desc, pb.desc, ms, N.ptr(bias_t), N.ptr(out), N.ptr(ws), ws.numel(),
+                                N.stream_of(device)), "tc_gemm")
+        else:
+            N.check(lib.tc_gemm_encoded(pa.desc, pb.desc, N.ptr(enc), enc.numel(), ms, N.ptr(bias_t), N.ptr(out),
+                                        N.ptr(ws), ws.numel(), N.stream_of(device)), "tc_gemm_encoded")
     return out
+
+
+def _tensor_state(t) -> tuple | None:
+    """What an encoding derived from ``t`` depends on: which tensor, its storage, its layout and its
+    in-place version counter (TriCast's ``mma/operand.py:21-26`` rule; edits through ``.data`` or
+    inside ``torch.inference_mode`` are not versioned, as there)."""
+    if t is None:
+        return None
+    version = None if t.is_inference() else t._version
+    return id(t), t.data_ptr(), tuple(t.shape), t.stride(), version
+
+
+def _encoded_b(a, b, spec, apply, pa, pb, ms):
+    """The fast path's encoding of ``b``, kept on the operand object between calls the way TriCast
+    keeps a weight operand's K-major copy (``mma/operand.py:66-75``): encoded on first use for this
+    spec and kind of A, reused while B's tensors are unchanged. None when the pair's fast path takes
+    no pre-encoded B (or the object cannot hold a cache), in which case tc_gemm encodes per call."""
+    cache = getattr(b, "__dict__", None)
+    if cache is None:
+        return None
+    encodings = cache.setdefault("_tc_b_encodings", {})
+    key = (repr(spec), apply, a.rows > 16, repr(a.fmt), a.scale_kind, int(a.k_domain or 0), repr(a.scale_fmt))
+    state = (_tensor_state(b.values), _tensor_state(b.scale), _tensor_state(b.alpha))
+    hit = encodings.get(key)
+    if hit is not None and hit[0] == state:
+        return hit[1]
+    lib = N.lib()
+    nbytes = lib.tc_encode_b_bytes(pa.desc, pb.desc, ms)
+    enc = None
+    if nbytes:
+        enc = torch.empty(nbytes, device=b.values.device, dtype=torch.uint8)
+        N.check(lib.tc_encode_b(pa.desc, pb.desc, ms, N.ptr(enc), nbytes, N.stream_of(b.values.device)),
+                "tc_encode_b")
+    encodings[key] = (state, enc)
+    return enc
 
 
 def exact_fallbacks(device=None) -> int:

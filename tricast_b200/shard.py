@@ -82,6 +82,28 @@ def quantize_shard(x: torch.Tensor, spec, group=None):
     return quantize_into(x, spec, tensor_amax=amax)[0]
 
 
+def quantize_operands(a: torch.Tensor, spec_a, b_shard: torch.Tensor, spec_b, group=None):
+    """(QTensor of all of ``a``, QTensor of this rank's shard of ``b``) for one N-column slab of a GEMM.
+    When ``b``'s scheme needs the whole tensor's amax, the all-reduce of the shards' amax bits is
+    issued asynchronously and ``a`` is quantized while it is in flight."""
+    import torch.distributed as dist
+
+    if not needs_tensor_amax(spec_b) or not (dist.is_initialized() and dist.get_world_size(group) > 1):
+        return quantize_into(a, spec_a)[0], quantize_shard(b_shard, spec_b, group)
+    x2d = b_shard.reshape(-1, b_shard.shape[-1]).contiguous()
+    bits = torch.zeros((), dtype=torch.int32, device=b_shard.device)
+    with torch.cuda.device(b_shard.device):
+        N.check(N.lib().tc_tensor_amax_bits(N.ptr(x2d), N.dtype_code(x2d.dtype), x2d.numel(), N.ptr(bits),
+                                            N.stream_of(b_shard.device)), "tc_tensor_amax_bits")
+    work = dist.all_reduce(bits, op=dist.ReduceOp.MAX, group=group, async_op=True)
+    qa = quantize_into(a, spec_a)[0]
+    work.wait()  # the current stream waits for the reduction; the host does not
+    amax = bits.view(torch.float32)
+    if spec_b.granularity == "tensor":
+        return qa, quantize_into(b_shard, spec_b, amax=amax)[0]
+    return qa, quantize_into(b_shard, spec_b, tensor_amax=amax)[0]
+
+
 def gather_columns(slab: torch.Tensor, n: int, group=None) -> torch.Tensor:
     """The full ``[M, n]`` output from every rank's ``[M, slab]`` column slab (one all-gather)."""
     import torch.distributed as dist
@@ -99,4 +121,4 @@ def gather_columns(slab: torch.Tensor, n: int, group=None) -> torch.Tensor:
     return torch.cat([parts[r, : e - s] for r, (s, e) in enumerate(widths)]).T.contiguous()
 
 
-__all__ = ["column_slab", "needs_tensor_amax", "shard_amax", "reduce_amax_bits", "quantize_shard", "gather_columns"]
+__all__ = ["column_slab", "needs_tensor_amax", "shard_amax", "reduce_amax_bits", "quantize_shard", "quantize_operands", "gather_columns"]
