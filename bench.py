@@ -253,6 +253,105 @@ def gemm_step(name: str, dev, world: int = 1, rank: int = 0, size: int = 0):
     return step, m * n * k, (m, n, k), (a_cpu, b_cpu[s:e].contiguous())
 
 
+class GraphedStep:
+    """One rank's step of a config, replayed from CUDA graphs over static device inputs: the same
+    public calls as :func:`gemm_step` (quantize A, quantize this rank's slab of B, emulated GEMM),
+    captured once, so that a step costs the host a few graph launches instead of the calls' Python
+    and ctypes work (which otherwise bounds the short per-rank steps of a split over many GPUs).
+    Where B's scheme needs the whole B's amax and there are several ranks, the step is three graphs:
+    the slab's amax bits; A's quantization, replayed while the NCCL all-reduce of the bits runs; B's
+    quantization against the reduced amax and the GEMM."""
+
+    def __init__(self, name: str, dev, world: int, rank: int, host_inputs):
+        import torch
+        import torch.distributed as dist
+
+        from tricast_b200 import _native as N
+        from tricast_b200 import as_operand, gemm_triton, workloads
+        from tricast_b200.quantize import quantize_into
+        from tricast_b200.shard import needs_tensor_amax, quantize_shard
+        from tricast_b200.spec import PRESETS, SCHEMES
+
+        schemes = {"cfg2": ("nvfp4", "nvfp4"), "cfg3": ("fp8_tensor", "fp8_tensor"),
+                   "cfg4": ("int8_row", "int4_g128_zp")}[name]
+        sa, sb = SCHEMES[schemes[0]], SCHEMES[schemes[1]]
+        spec = {"cfg2": lambda: PRESETS["nvidia_blackwell_fp4"].with_(out_format="fp32"),
+                "cfg3": lambda: PRESETS["nvidia_hopper_fp8"].with_(out_format="fp32"),
+                "cfg4": workloads.cfg4_spec}[name]()
+        self.inputs = [h.to(dev) for h in host_inputs]
+        xa, xb = self.inputs
+        self.world, self.dev = world, dev
+        self.split = world > 1 and needs_tensor_amax(sb)
+        self.bits = torch.zeros((), dtype=torch.int32, device=dev)
+        state = {}
+
+        def amax_bits():
+            self.bits.zero_()
+            x2d = xb.reshape(-1, xb.shape[-1])
+            N.check(N.lib().tc_tensor_amax_bits(N.ptr(x2d), N.dtype_code(x2d.dtype), x2d.numel(), N.ptr(self.bits),
+                                                N.stream_of(dev)), "tc_tensor_amax_bits")
+
+        def quant_a():
+            state["qa"] = quantize_into(xa, sa)[0]
+
+        def quant_b_gemm():
+            if self.split:
+                amax = self.bits.view(torch.float32)
+                qb = quantize_into(xb, sb, **({"amax": amax} if sb.granularity == "tensor" else {"tensor_amax": amax}))[0]
+            else:
+                qb = quantize_shard(xb, sb)
+            qa = state["qa"]
+            ops = workloads.cfg4_operands(qa, qb) if name == "cfg4" else (as_operand(qa, compact=True),
+                                                                          as_operand(qb, compact=True))
+            state["out"] = gemm_triton(*ops, spec)
+
+        def whole():
+            quant_a()
+            quant_b_gemm()
+
+        def eager():
+            if self.split:
+                amax_bits()
+                dist.all_reduce(self.bits, op=dist.ReduceOp.MAX)
+                whole()
+            else:
+                whole()
+
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            eager()
+            n0 = N.lib().tc_launch_count()
+            eager()
+            self.launches_per_step = N.lib().tc_launch_count() - n0  # the library kernels of one step
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        parts = [amax_bits, quant_a, quant_b_gemm] if self.split else [whole]
+        self.graphs = []
+        for part in parts:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                part()
+            self.graphs.append(graph)
+        self.out = state["out"]
+
+    def __call__(self):
+        import torch.distributed as dist
+
+        if not self.split:
+            self.graphs[0].replay()
+            return self.out
+        self.graphs[0].replay()
+        work = dist.all_reduce(self.bits, op=dist.ReduceOp.MAX, async_op=True)
+        self.graphs[1].replay()  # A's quantization runs while the all-reduce is in flight
+        work.wait()
+        self.graphs[2].replay()
+        return self.out
+
+    def release(self) -> None:
+        self.graphs = []
+
+
 def time_steps(step, dev, steps: int, warmup: int, world: int = 1) -> list:
     """Device time of each of ``steps`` calls (after ``warmup``), a 512 MiB L2 flush before each one
     outside its events, all enqueued back to back; barrier + synchronize on both sides."""
@@ -419,6 +518,79 @@ def measure_tricast_triton(dev, ours_cfg2=None) -> dict:
     return out
 
 
+def measure_reference_rows(dev) -> dict:
+    """TriCast's own MMA benchmark (``scripts/bench/bench_mma_vs_nadpe.py``: FP8 E4M3 operands
+    ``randn * 2`` with unit tensor scales, bf16 output; CoFDA F=13 CS=32, decoupled CoFDA F=13 CS=32
+    F2=23, GDFS G=32 F=25 GS=16 KT=32; shapes 2048x1024x3072, 2048x3072x1024, 4096^3), each row run by
+    this library and by TriCast's Triton backend on this GPU with that script's protocol, outputs
+    compared bit for bit. Seeded like the script (torch.manual_seed(42), operands drawn on the GPU)."""
+    import torch
+
+    from tricast_b200 import gemm_triton
+    from tricast_b200.formats import FP32, get_format
+    from tricast_b200.operand import Operand
+    from tricast_b200.spec import MMASpec
+
+    tri = tricast_module()
+    configs = [("hopper CoFDA F=13 CS=32", dict(algorithm="cofda", f_bits=13, chunk_size=32)),
+               ("CoFDA C-decoupled F=13 CS=32", dict(algorithm="cofda", f_bits=13, chunk_size=32, c_mode="decoupled",
+                                                     f2_bits=23)),
+               ("GDFS G=32 F=25 GS=16", dict(algorithm="gdfs", f_bits=25, g_bits=32, group_size=16, k_tile=32))]
+    shapes = [(2048, 1024, 3072), (2048, 3072, 1024), (4096, 4096, 4096)]
+
+    def timed(fn, warmup=3, repeat=5):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        times = []
+        for _ in range(repeat):
+            e0, e1 = event_pair()
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            times.append(e0.elapsed_time(e1))
+        return times
+
+    torch.manual_seed(42)
+    rows = []
+    fp8 = get_format("fp8_e4m3")
+    for m, n, k in shapes:
+        a8 = (torch.randn(m, k, device=dev) * 2).to(torch.float8_e4m3fn)
+        w8 = (torch.randn(n, k, device=dev) * 2).to(torch.float8_e4m3fn)
+        one = torch.ones((), device=dev)
+        a_op, w_op = Operand(a8.float(), fp8, one, FP32, "tensor"), Operand(w8.float(), fp8, one, FP32, "tensor")
+        for label, kw in configs:
+            spec = MMASpec(kw.pop("algorithm"), out_format="bf16", **kw)
+            kw["algorithm"] = spec.algorithm
+            mine = gemm_triton(a_op, w_op, spec)
+            t = stats_ms(timed(lambda: gemm_triton(a_op, w_op, spec)))
+            row = {"shape": [m, n, k], "config": label, "b200_tmacs": m * n * k / (t["median"] * 1e-3) / 1e12,
+                   "b200_ms": t}
+            if tri is not None:
+                from tricast import BF16 as T_BF16
+                from tricast import FP8_E4M3 as T_FP8
+                from tricast import FP32 as T_FP32
+                from tricast import MMASpec as T_MMASpec
+                from tricast.kernels.mma import gemm_triton as t_gemm_triton
+                from tricast.mma.operand import Operand as T_Operand
+
+                ta = T_Operand(a8.float(), T_FP8, one, T_FP32, "tensor")
+                tw = T_Operand(w8.float(), T_FP8, one, T_FP32, "tensor")
+                tkw = {key: v for key, v in kw.items() if key != "algorithm"}
+                tspec = T_MMASpec(kw["algorithm"], out_format=T_BF16, **tkw)
+                try:
+                    theirs = t_gemm_triton(ta, tw, tspec)
+                    tt = stats_ms(timed(lambda: t_gemm_triton(ta, tw, tspec)))
+                    row.update({"triton_tmacs": m * n * k / (tt["median"] * 1e-3) / 1e12, "triton_ms": tt,
+                                "bit_identical": bool(torch.equal(theirs.view(torch.int16), mine.view(torch.int16)))})
+                except Exception as exc:  # JIT or launch failure of the reference is reported
+                    row["triton_error"] = repr(exc)[:300]
+            rows.append(row)
+    return {"source": "TriCast scripts/bench/bench_mma_vs_nadpe.py rows (A100 published: CoFDA 0.15, GDFS 0.11 "
+                      "TMAC/s)", "rows": rows}
+
+
 # ------------------------------------------------------------------------------- the CPU reference
 class CpuSample:
     """One bounded sample of the cfg2 step on the host cores: a ``rows`` x ``cols`` slab of the output
@@ -514,46 +686,42 @@ def run_reference(args) -> None:
 
 
 # ------------------------------------------------------------------------------------ end to end
-def e2e_pipelined(step, host_inputs, dev, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
+def e2e_pipelined(steppers, host_inputs, dev, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
     """The step end to end from pinned host memory, as a serving loop runs it: every step copies its
-    inputs host -> device (a copy stream), runs the public-API step (the compute stream) and copies its
-    result device -> host (a third stream). Two device input buffers and two pinned host output
-    buffers alternate, so step i + 1's upload and step i - 1's download overlap step i's compute; the
-    ordering is by CUDA events only. Returns (ms per step over the K timed steps, from the first
-    upload's start to the last download's end; H2D bytes per step; D2H bytes per step)."""
+    inputs host -> device (a copy stream), runs the step (the compute stream) and copies its result
+    device -> host (a third stream). Two steppers (each a :class:`GraphedStep` with its own static
+    inputs and output) and two pinned host outputs alternate, so step i + 1's upload and step i - 1's
+    download overlap step i's compute; the ordering is by CUDA events only. Returns (ms per step over
+    the K timed steps, from the first upload's start to the last download's end; H2D bytes per step;
+    D2H bytes per step)."""
     import torch
     import torch.distributed as dist
 
     comp = torch.cuda.current_stream(dev)
     up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    dev_in = [[torch.empty_like(h, device=dev) for h in host_inputs] for _ in range(2)]
-    host_out = [None, None]
+    host_out = [torch.empty(st.out.shape, dtype=st.out.dtype, pin_memory=True) for st in steppers]
     in_ready = [torch.cuda.Event(), torch.cuda.Event()]
     in_free = [torch.cuda.Event(), torch.cuda.Event()]
-    d2h_bytes = 0
+    out_free = [torch.cuda.Event(), torch.cuda.Event()]
 
     def run(n: int) -> None:
-        nonlocal d2h_bytes
         for i in range(n):
             j = i & 1
+            st = steppers[j]
             if i >= 2:
-                up.wait_event(in_free[j])
+                up.wait_event(in_free[j])    # step i - 2 is done reading these inputs
+                comp.wait_event(out_free[j])  # and its result has been downloaded
             with torch.cuda.stream(up):
-                for d, h in zip(dev_in[j], host_inputs):
+                for d, h in zip(st.inputs, host_inputs):
                     d.copy_(h, non_blocking=True)
                 in_ready[j].record(up)
             comp.wait_event(in_ready[j])
-            out = step(*dev_in[j])
+            out = st()
             in_free[j].record(comp)
-            done = torch.cuda.Event()
-            done.record(comp)
-            if host_out[j] is None:
-                host_out[j] = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-            down.wait_event(done)
+            down.wait_stream(comp)
             with torch.cuda.stream(down):
                 host_out[j].copy_(out, non_blocking=True)
-            out.record_stream(down)
-            d2h_bytes = out.numel() * out.element_size()
+                out_free[j].record(down)
 
     run(warmup)
     torch.cuda.synchronize(dev)
@@ -563,12 +731,11 @@ def e2e_pipelined(step, host_inputs, dev, steps: int, warmup: int, world: int) -
     start, end = event_pair()
     start.record(up)
     run(steps)
-    down.wait_stream(up)
     end.record(down)
     end.synchronize()
     torch.cuda.synchronize(dev)
     h2d = sum(h.numel() * h.element_size() for h in host_inputs)
-    return start.elapsed_time(end) / steps, h2d, d2h_bytes
+    return start.elapsed_time(end) / steps, h2d, steppers[0].out.numel() * steppers[0].out.element_size()
 
 
 # ------------------------------------------------------------------------------------ the headline
@@ -586,24 +753,25 @@ def run_b200(args) -> None:
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
-    from tricast_b200 import _native
     from tricast_b200.sweep import SweepConfig, measure_costs, run_sweep
 
-    lib = _native.lib()
     step, macs, _, host_inputs = gemm_step("cfg2", dev, world, rank)
     stream = torch.cuda.current_stream(dev)
     gemm_events = []
+    # The step's public calls captured as CUDA graphs (GraphedStep); two more for the end-to-end
+    # pipeline's double-buffered inputs.
+    graphed = [GraphedStep("cfg2", dev, world, rank, host_inputs) for _ in range(3)]
+    gstep = graphed[0]
 
     # The headline: K steps enqueued back to back (no host wait per step), each with its own events,
     # a 512 MiB L2 flush between steps outside them; max over ranks.
     for _ in range(args.warmup):
-        step()
+        gstep()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     with Clocks(local) as clocks:
-        launches0 = lib.tc_launch_count()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
@@ -612,15 +780,16 @@ def run_b200(args) -> None:
             flush.fill_(1)
             s0, s1 = event_pair()
             s0.record(stream)
-            step()
+            gstep()
             s1.record(stream)
             step_events.append((s0, s1))
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
-        launches = lib.tc_launch_count() - launches0
-        # The GEMM call alone (operand encoders + GDFS kernel) on operands quantized beforehand, with
-        # events around it on the stream it launches on.
+        launches = gstep.launches_per_step * args.steps  # graph replays launch the captured kernels
+        # The GEMM call alone on operands quantized beforehand, with events around it on the stream it
+        # launches on. B's encoding is kept on its operand between calls (as a weight's is), so the
+        # events span A's encoders and the GDFS kernel.
         ops = step.operands()
         for _ in range(args.steps):
             flush.fill_(1)
@@ -633,7 +802,7 @@ def run_b200(args) -> None:
         del ops
         # End to end through the public API from pinned host memory.
         pinned = [h.pin_memory() for h in host_inputs]
-        t_e2e, h2d, d2h = e2e_pipelined(step, pinned, dev, args.steps, args.warmup, world)
+        t_e2e, h2d, d2h = e2e_pipelined(graphed[1:], pinned, dev, args.steps, args.warmup, world)
         # Layer sweep (cfg5): per-shape costs measured at full size (which also warms every shape
         # up), LPT on them, then the device-timed sweep, max over ranks.
         cfg = SweepConfig()
@@ -673,6 +842,8 @@ def run_b200(args) -> None:
                                 "streams with double-buffered inputs and outputs; timed from the first upload to "
                                 "the last download; bytes summed over ranks"},
             "gpu_launches": int(launches),
+            "graphs": "each step replays CUDA graphs of its public calls; gpu_launches = the library kernels "
+                      "one step launches (counted on an eager step) x steps",
             "roofline": {"bound": "alu", "achieved": achieved, "peak": peak_gmacs, "unit": "GMAC/s",
                          "frac": achieved / peak_gmacs, "traffic": GDFS_TRAFFIC_BYTES if world == 1 else None,
                          "issue_util": GDFS_ISSUE_UTIL,
@@ -697,12 +868,15 @@ def run_b200(args) -> None:
             line["aux_decode"] = measure_decode(dev)
             if not args.quick:
                 line["aux_triton"] = measure_tricast_triton(dev, step)
+                line["aux_reference_rows"] = measure_reference_rows(dev)
             if not args.no_cpu_baseline:
                 line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
     from tricast_b200.sweep import release_graphs
 
     release_graphs()
+    for g in graphed:
+        g.release()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -716,7 +890,7 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true", help="skip the slow auxiliary measurements (Triton, cfg3)")
-    ap.add_argument("--workload", default="all", choices=["all", "cfg2step", "cfg1", "cfg3", "cfg4", "decode", "triton"],
+    ap.add_argument("--workload", default="all", choices=["all", "cfg2step", "cfg1", "cfg3", "cfg4", "decode", "triton", "rows"],
                     help="run only that measurement on one GPU (for profiling)")
     ap.add_argument("--cube", type=int, default=0,
                     help="with --workload cfg3: run an M = N = K = CUBE case instead of 8192 (profiling)")
@@ -739,6 +913,8 @@ def main() -> None:
             print(json.dumps(measure_decode(dev, calls=args.steps)))
         elif args.workload == "triton":
             print(json.dumps(measure_tricast_triton(dev)))
+        elif args.workload == "rows":
+            print(json.dumps(measure_reference_rows(dev)))
         else:
             print(json.dumps(measure_gemm_config(dev, args.workload, args.steps, args.warmup, size=args.cube)))
         return

@@ -58,5 +58,6 @@ def test_layer_report_on_library_equals_reference_backend(model, recipe):
                        samples=2, seqlen=48)
     assert _native.lib().tc_launch_count() - launches >= 2 * 14 * 2, "the report's layers did not run on tricast_b200"
     assert len(emu["layers"]) == 14 and all(e["status"] == "measured" for e in emu["layers"])
-    assert emu["patch_report"]["patched"] == ref["patch_report"]["patched"]
+    names = lambda report: [name for name, _ in report["patch_report"]["patched"]]  # noqa: E731
+    assert names(emu) == names(ref)
     assert _strip(emu) == _strip(ref)

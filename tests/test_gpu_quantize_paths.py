@@ -224,3 +224,23 @@ def test_mse_and_percentile_scales_vs_oracle(name, shape):
             assert bits_equal(g, np.asarray(w)), f"{name} {field}: {first_mismatch(g, np.asarray(w))}"
     dq = ex.dequant.cpu().numpy()
     assert bits_equal(dq, oracle_dequantize(want)), f"{name} dequant: {first_mismatch(dq, oracle_dequantize(want))}"
+
+
+@pytest.mark.parametrize("K", [2048, 4096, 4097])
+@pytest.mark.parametrize("spec", [QuantSpec("fp8_e4m3", "row"), QuantSpec("int8", "row"), QuantSpec("fp8_e4m3", "tensor"),
+                                  QuantSpec("int4", "row"), QuantSpec("fp4_e2m1", "row"),
+                                  QuantSpec("uint4", "row", scale=ScaleSpec("fp16"), zero_point="int", mma_input="dequant")],
+                         ids=lambda s: f"{s.format.name}-{s.granularity}{'-zp' if s.zero_point != 'none' else ''}")
+def test_single_row_tensors_take_the_grid_wide_pass(spec, K):
+    """A decode step's one-row activation is a single scale domain: it runs through the grid-wide
+    tensor pipeline (not one block on one row) and must equal the oracle, codes included."""
+    g = torch.Generator().manual_seed(K)
+    x = torch.randn(1, K, generator=g) * 3
+    x[0, 5] = 40.0
+    q, extras = quantize_into(x.cuda(), spec, want_codes=True, want_dequant=True)
+    want = oracle_quantize(x.numpy(), spec)
+    assert bits_equal(q.values.float().cpu().numpy(), want.values), first_mismatch(q.values.float().cpu().numpy(), want.values)
+    assert bits_equal(q.scale.cpu().numpy().reshape(-1), np.asarray(want.scale, np.float32).reshape(-1))
+    if spec.zero_point != "none":
+        assert bits_equal(q.zero_point.cpu().numpy().reshape(-1), np.asarray(want.zero_point, np.float32).reshape(-1))
+    assert bits_equal(extras.dequant.cpu().numpy(), np.asarray(oracle_dequantize(want)).reshape(extras.dequant.shape))

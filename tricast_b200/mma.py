@@ -188,7 +188,10 @@ def _encoded_b(a, b, spec, apply, pa, pb, ms):
     if cache is None:
         return None
     encodings = cache.setdefault("_tc_b_encodings", {})
-    key = (repr(spec), apply, a.rows > 16, repr(a.fmt), a.scale_kind, int(a.k_domain or 0), repr(a.scale_fmt))
+    # What B's encoding depends on besides B: the C-level spec (scale application included) and the
+    # kind of A (more or fewer than 17 rows, its format and K-scale layout).
+    d = pa.desc
+    key = (bytes(ms), a.rows > 16, bytes(d.fmt), d.scale_kind, d.has_scale_fmt, bytes(d.scale_fmt), d.k_domain)
     state = (_tensor_state(b.values), _tensor_state(b.scale), _tensor_state(b.alpha))
     hit = encodings.get(key)
     if hit is not None and hit[0] == state:
