@@ -404,3 +404,69 @@ def test_int_tensor_core_path(shape):
     assert exact_fallbacks() == before, "the tensor-core kernel declined or timed out"
     want = _oracle_gemm(ia, ib, spec)
     assert bits_equal(got, want), first_mismatch(got, want)
+
+
+# ---------------------------------------------------------------- GDFS on narrow float grids
+GDFS_NARROW = [
+    # TriCast's own benchmark row (scripts/bench/bench_mma_vs_nadpe.py:31-32)
+    dict(f_bits=25, g_bits=32, group_size=16, k_tile=32),
+    dict(f_bits=25, g_bits=32, group_size=16, k_tile=64),
+    dict(f_bits=23, g_bits=10, group_size=16, k_tile=16),
+    dict(f_bits=13, g_bits=8, group_size=8, k_tile=32),       # precision below fp32's: F < 23
+    dict(f_bits=35, g_bits=24, group_size=32, k_tile=64, norm_rounding="rne"),
+]
+
+
+@pytest.mark.parametrize("kw", GDFS_NARROW, ids=lambda kw: "-".join(f"{k[0]}{v}" for k, v in kw.items()))
+@pytest.mark.parametrize("scheme,shape", [("fp8_tensor", (70, 50, 160)), ("fp8_row", (33, 65, 96)),
+                                          ("mxfp8_e4m3", (64, 64, 256)), ("mxfp8_e5m2", (40, 72, 128))])
+def test_gdfs_narrow_kernel_matches_oracle(kw, scheme, shape):
+    """The fast GDFS kernel for narrow float grids (tc_gemm_gdfs.cu) on FP8 E4M3 / E5M2 operands with
+    tensor, row and E8M0 group scales, ragged shapes and K tails, bit for bit with the oracle, and
+    without falling back to the exact generic kernel."""
+    if scheme not in SCHEMES:
+        pytest.skip(f"{scheme} is not a registered scheme")
+    m, n, k = shape
+    spec = MMASpec("gdfs", out_format="fp32", **kw)
+    if scheme == "mxfp8_e4m3" and kw["group_size"] > 32:
+        pytest.skip("a GDFS group may not cross a 32-wide E8M0 scale domain")
+    a = _quantized(scheme, m, k, 1, outliers=3)
+    b = _quantized(scheme, n, k, 2, scale=0.02)
+    before = exact_fallbacks()
+    got = gemm_triton(a, b, spec).cpu().numpy()
+    assert exact_fallbacks() == before, "the fast GDFS kernel declined finite on-grid operands"
+    want = _oracle_gemm(a, b, spec)
+    assert bits_equal(got, want), f"{spec}: {first_mismatch(got, want)}"
+
+
+def test_gdfs_narrow_kernel_cancelling_groups():
+    """A group whose aligned sum cancels to exactly zero takes no part in the tile's FDA. Here the
+    third group of 16 (k 32..47) has the largest products but pairs every product with its negation,
+    so it sets the tile's provisional exponent and then drops out: those outputs redo their tile step
+    with the exponent of the remaining terms."""
+    g = torch.Generator().manual_seed(3)
+
+    def fp8(x):
+        return x.to(torch.float8_e4m3fn).float()
+
+    m, n = 8, 16
+    a = fp8(torch.randn(m, 64, generator=g) * 2)
+    b = fp8(torch.randn(n, 64, generator=g) * 2)
+    half_a = fp8(torch.randn(m, 8, generator=g) * 64)
+    half_b = fp8(torch.randn(n, 8, generator=g) * 64)
+    a[:, 32:48] = torch.cat([half_a, half_a], dim=1)
+    b[:, 32:48] = torch.cat([half_b, -half_b], dim=1)
+    b[:, 48:64] *= 0.01  # the group that remains after the cancellation is small
+    b = fp8(b)
+    from tricast_b200.formats import FP32, get_format
+
+    one = torch.ones((), device="cuda")
+    opa = Operand(a.cuda(), get_format("fp8_e4m3"), one, FP32, "tensor")
+    opb = Operand(b.cuda(), get_format("fp8_e4m3"), one, FP32, "tensor")
+    for kt in (32, 64):
+        spec = MMASpec("gdfs", f_bits=25, g_bits=32, group_size=16, k_tile=kt, out_format="fp32")
+        before = exact_fallbacks()
+        got = gemm_triton(opa, opb, spec).cpu().numpy()
+        assert exact_fallbacks() == before
+        want = _oracle_gemm(opa, opb, spec)
+        assert bits_equal(got, want), f"k_tile={kt}: {first_mismatch(got, want)}"

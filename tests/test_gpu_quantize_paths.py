@@ -237,7 +237,9 @@ def test_single_row_tensors_take_the_grid_wide_pass(spec, K):
     g = torch.Generator().manual_seed(K)
     x = torch.randn(1, K, generator=g) * 3
     x[0, 5] = 40.0
-    q, extras = quantize_into(x.cuda(), spec, want_codes=True, want_dequant=True)
+    four_bit = spec.format.name in ("int4", "uint4", "fp4_e2m1")
+    codes = not (four_bit and K % 2)  # packed 4-bit codes need an even element count
+    q, extras = quantize_into(x.cuda(), spec, want_codes=codes, want_dequant=True)
     want = oracle_quantize(x.numpy(), spec)
     assert bits_equal(q.values.float().cpu().numpy(), want.values), first_mismatch(q.values.float().cpu().numpy(), want.values)
     assert bits_equal(q.scale.cpu().numpy().reshape(-1), np.asarray(want.scale, np.float32).reshape(-1))

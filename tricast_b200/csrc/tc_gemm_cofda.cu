@@ -30,88 +30,12 @@
 #include <cstring>
 #include <string>
 
-#include "tc_bulk.cuh"
-#include "tc_cofda.cuh"
+#include "tc_cofda_tile.cuh"
 
 namespace tc {
 namespace cofda {
 
-constexpr int kTile = 64;     // rows of A and columns of B per CTA
 constexpr int kStages = 3;
-
-struct EncodeArgs {
-  const void *v;
-  int dt;
-  int64_t rows, K, rows_pad, nchunks;
-  int CS;
-  Fmt f;
-  const float *scale;  // product-mode pow2 K scales folded into the values, or nullptr
-  int64_t nkd;
-  int kd;
-  Fmt sf;
-  int field0;
-  void *val;           // [tile][chunk][k][kTile], float or double
-  uint32_t *exp;       // A: [tile][chunk][k][kTile/2] (pairs of rows); B: [tile][chunk][k][kTile] (duplicated)
-  int side;
-  int32_t *flag;
-};
-
-template <class T>
-__global__ void __launch_bounds__(256) encode_kernel(EncodeArgs e) {
-  const int64_t pairs = e.rows_pad / 2;
-  const int64_t total = pairs * e.nchunks * e.CS;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  bool bad = false;
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
-    const int64_t rp = idx % (kTile / 2);            // row pair inside the tile
-    int64_t rest = idx / (kTile / 2);
-    const int64_t kk = rest % e.CS;
-    rest /= e.CS;
-    const int64_t chunk = rest % e.nchunks;
-    const int64_t tile = rest / e.nchunks;
-    const int64_t k = chunk * e.CS + kk;
-    float vals[2];
-    int exps[2];
-    for (int h = 0; h < 2; ++h) {
-      const int64_t r = tile * kTile + rp * 2 + h;
-      float v = 0.0f;
-      int ex = kZeroExp;
-      if (r < e.rows && k < e.K) {
-        v = load_as_float(e.v, e.dt, r * e.K + k);
-        if (!decode_elem(v, e.f, ex)) bad = true;
-        if (e.scale) {
-          float s = e.scale[r * e.nkd + k / e.kd];
-          Term ts = decode_term(s, e.sf);
-          bool zero = ts.zero || (e.field0 && f2u(s) == 0x00400000u);
-          if (ts.nan || ts.inf || (!zero && (ts.sig != 1 || ts.neg))) bad = true;  // pow2 scales only
-          if (zero || ex == kZeroExp) {
-            v = 0.0f;
-            ex = kZeroExp;
-          } else {
-            // Folded labels in [-50, 60]: products stay normal fp32 values, and a chunk with a non-zero
-            // product has emax >= -100, so its scale 2**(F - emax) is a normal fp32 power.
-            if (ts.exp < -60 || ts.exp > 60 || ex + ts.exp < -50 || ex + ts.exp > 60) bad = true;
-            v = ldexpf(v, ts.exp);
-            ex += ts.exp;
-          }
-        }
-      }
-      if (ex == kZeroExp) v = 0.0f;
-      vals[h] = v;
-      exps[h] = ex;
-    }
-    const int64_t base = ((tile * e.nchunks + chunk) * e.CS + kk) * kTile;
-    static_cast<T *>(e.val)[base + rp * 2] = (T)vals[0];
-    static_cast<T *>(e.val)[base + rp * 2 + 1] = (T)vals[1];
-    if (e.side == 0) {
-      e.exp[base / 2 + rp] = ((uint32_t)exps[0] & 0xFFFFu) | ((uint32_t)exps[1] << 16);
-    } else {
-      e.exp[base + rp * 2] = ((uint32_t)exps[0] & 0xFFFFu) | ((uint32_t)exps[0] << 16);
-      e.exp[base + rp * 2 + 1] = ((uint32_t)exps[1] & 0xFFFFu) | ((uint32_t)exps[1] << 16);
-    }
-  }
-  if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicExch(e.flag, 1);
-}
 
 struct Args {
   const void *av, *bv;           // staged operand values (float or double)
@@ -126,14 +50,6 @@ struct Args {
   const int32_t *flag;
   int32_t *status;
   int wait_polls;  // poll limit of the pipeline waits (negative: default)
-};
-
-template <int CS, class T>
-struct Stage {
-  T av[CS][kTile];
-  T bv[CS][kTile];
-  uint32_t be[CS][kTile];
-  uint32_t ae[CS][kTile / 2];
 };
 
 template <int CS, bool RNE, class T>
@@ -329,7 +245,6 @@ struct CofdaPlan {
   size_t off[4], total, flag_off;
 };
 
-static bool narrow_float(const Fmt &f) { return f.kind == 0 && f.mbits <= 3 && f.emax <= 15 && f.emin >= -14; }
 
 static CofdaPlan plan_cofda(const GemmDesc &g) {
   CofdaPlan p;
@@ -337,7 +252,7 @@ static CofdaPlan plan_cofda(const GemmDesc &g) {
   if (g.alg != ALG_COFDA) return p;
   if (g.decoupled && !g.PI && (g.F2 < 1 || g.F2 > 50)) return p;  // the fp64 merge needs F2 <= 50
   if (g.CS != 8 && g.CS != 16 && g.CS != 32) return p;
-  if (!narrow_float(g.a.f) || !narrow_float(g.b.f)) return p;
+  if (!cofda::narrow_float(g.a.f) || !cofda::narrow_float(g.b.f)) return p;
   int width_bits = 0;
   while ((1 << width_bits) <= g.CS) ++width_bits;  // bit length of CS (covers CS + 1 terms)
   if (g.F + 2 + width_bits > 53) return p;

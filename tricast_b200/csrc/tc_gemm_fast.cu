@@ -493,6 +493,8 @@ int launch_cofda(const GemmDesc &g, void *workspace, size_t workspace_bytes, cud
 
 size_t int_workspace(const GemmDesc &g);
 int launch_fma(const GemmDesc &g, cudaStream_t s);
+size_t gdfs_workspace(const GemmDesc &g);
+int launch_gdfs(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
 int launch_int(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s);
 
 int launch_fp4_gemm_tc(const fp4::GemmArgs &args, int ng, cudaStream_t s);
@@ -506,7 +508,8 @@ size_t fast_workspace(const GemmDesc &g) {
   Fp4Plan p = plan_fp4(g);
   if (p.ok) return g.M <= kGemvMaxM ? fp4_gemv_workspace(g, p.ng) : p.total;
   size_t w = int_workspace(g);
-  return w ? w : cofda_workspace(g);
+  if (!w) w = cofda_workspace(g);
+  return w ? w : gdfs_workspace(g);
 }
 
 template <int NG, bool RNE>
@@ -633,6 +636,8 @@ int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
     int st = launch_int(g, workspace, workspace_bytes, s);
     if (st != TC_UNSUPPORTED) return st;
     st = launch_cofda(g, workspace, workspace_bytes, s);
+    if (st != TC_UNSUPPORTED) return st;
+    st = launch_gdfs(g, workspace, workspace_bytes, s);
     if (st != TC_UNSUPPORTED) return st;
     return launch_fma(g, s);
   }

@@ -910,7 +910,8 @@ static int make_plan(const void *x, int32_t x_dtype, int64_t rows, int64_t K, co
   else if (searched) pl.path = PATH_GENERAL;
   // A single domain of more than a few thousand elements (a whole tensor, or the one row of a decode
   // step's activation) takes the grid-wide tensor pipeline; the row pass runs one block per row.
-  else if (p.nr == 1 && p.nc == 1 && rows * K >= 2048) pl.path = PATH_TENSOR;
+  else if (p.nr == 1 && p.nc == 1 && rows * K >= 2048 && (!out->codes || p.code_bits == 8 || (rows * K) % 2 == 0))
+    pl.path = PATH_TENSOR;  // (the flat element pass packs 4-bit codes in pairs)
   else if (p.dr == 1 && p.dc == K && (!out->codes || p.code_bits == 8 || K % 2 == 0)) pl.path = PATH_ROW;
   else if (p.nr == 1 && p.nc == 1) pl.path = PATH_TENSOR;
   else pl.path = PATH_GENERAL;
