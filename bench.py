@@ -518,12 +518,14 @@ def measure_tricast_triton(dev, ours_cfg2=None) -> dict:
     return out
 
 
-def measure_reference_rows(dev) -> dict:
+def measure_reference_rows(dev, only: str | None = None, triton: bool = True, shapes=None) -> dict:
     """TriCast's own MMA benchmark (``scripts/bench/bench_mma_vs_nadpe.py``: FP8 E4M3 operands
     ``randn * 2`` with unit tensor scales, bf16 output; CoFDA F=13 CS=32, decoupled CoFDA F=13 CS=32
     F2=23, GDFS G=32 F=25 GS=16 KT=32; shapes 2048x1024x3072, 2048x3072x1024, 4096^3), each row run by
     this library and by TriCast's Triton backend on this GPU with that script's protocol, outputs
-    compared bit for bit. Seeded like the script (torch.manual_seed(42), operands drawn on the GPU)."""
+    compared bit for bit. Seeded like the script (torch.manual_seed(42), operands drawn on the GPU).
+    ``only`` keeps the rows whose label starts with it; ``triton=False`` skips TriCast's side
+    (profiling one kernel)."""
     import torch
 
     from tricast_b200 import gemm_triton
@@ -531,12 +533,13 @@ def measure_reference_rows(dev) -> dict:
     from tricast_b200.operand import Operand
     from tricast_b200.spec import MMASpec
 
-    tri = tricast_module()
+    tri = tricast_module() if triton else None
     configs = [("hopper CoFDA F=13 CS=32", dict(algorithm="cofda", f_bits=13, chunk_size=32)),
                ("CoFDA C-decoupled F=13 CS=32", dict(algorithm="cofda", f_bits=13, chunk_size=32, c_mode="decoupled",
                                                      f2_bits=23)),
                ("GDFS G=32 F=25 GS=16", dict(algorithm="gdfs", f_bits=25, g_bits=32, group_size=16, k_tile=32))]
-    shapes = [(2048, 1024, 3072), (2048, 3072, 1024), (4096, 4096, 4096)]
+    configs = [c for c in configs if only is None or c[0].startswith(only)]
+    shapes = shapes or [(2048, 1024, 3072), (2048, 3072, 1024), (4096, 4096, 4096)]
 
     def timed(fn, warmup=3, repeat=5):
         for _ in range(warmup):
@@ -560,7 +563,8 @@ def measure_reference_rows(dev) -> dict:
         w8 = (torch.randn(n, k, device=dev) * 2).to(torch.float8_e4m3fn)
         one = torch.ones((), device=dev)
         a_op, w_op = Operand(a8.float(), fp8, one, FP32, "tensor"), Operand(w8.float(), fp8, one, FP32, "tensor")
-        for label, kw in configs:
+        for label, kw0 in configs:
+            kw = dict(kw0)
             spec = MMASpec(kw.pop("algorithm"), out_format="bf16", **kw)
             kw["algorithm"] = spec.algorithm
             mine = gemm_triton(a_op, w_op, spec)
@@ -890,7 +894,8 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true", help="skip the slow auxiliary measurements (Triton, cfg3)")
-    ap.add_argument("--workload", default="all", choices=["all", "cfg2step", "cfg1", "cfg3", "cfg4", "decode", "triton", "rows"],
+    ap.add_argument("--workload", default="all", choices=["all", "cfg2step", "cfg1", "cfg3", "cfg4", "decode", "triton", "rows",
+                                                      "gdfs_row"],
                     help="run only that measurement on one GPU (for profiling)")
     ap.add_argument("--cube", type=int, default=0,
                     help="with --workload cfg3: run an M = N = K = CUBE case instead of 8192 (profiling)")
@@ -915,6 +920,8 @@ def main() -> None:
             print(json.dumps(measure_tricast_triton(dev)))
         elif args.workload == "rows":
             print(json.dumps(measure_reference_rows(dev)))
+        elif args.workload == "gdfs_row":  # this library's GDFS G=32 row at 4096^3 alone
+            print(json.dumps(measure_reference_rows(dev, only="GDFS", triton=False, shapes=[(4096, 4096, 4096)])))
         else:
             print(json.dumps(measure_gemm_config(dev, args.workload, args.steps, args.warmup, size=args.cube)))
         return
