@@ -43,8 +43,8 @@ L2_FLUSH_BYTES = 512 << 20
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) and issue-slot share
 # (smsp__issue_active.avg.pct_of_peak_sustained_active / 100) of one gdfs_fp4_tc_kernel<4, 0> launch
 # on the cfg2 operands, from an ncu --set full capture of this build's kernel.
-GDFS_TRAFFIC_BYTES = 40_630_784 + 2_835_968
-GDFS_ISSUE_UTIL = 0.599
+GDFS_TRAFFIC_BYTES = 43_782_656 + 4_235_776
+GDFS_ISSUE_UTIL = 0.519
 CFG1_BYTES_PER_ELEM = 4 + 4 + 0.5 + 1 / 32  # fp32 in, fp32 dequant out, E2M1 nibble, E8M0 byte per 32
 REF_SLAB = (64, 1024)  # rows of A x rows of B per CPU sample step (full K)
 
@@ -376,6 +376,43 @@ def time_steps(step, dev, steps: int, warmup: int, world: int = 1) -> list:
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
+    return [a.elapsed_time(b) for a, b in events]
+
+
+def time_gemm_graphed(step, dev, steps: int, flush=None) -> list:
+    """Device time of the GEMM call alone, on operands quantized beforehand: B's encoding is made by a
+    first call and kept on its operand (as a weight's is), then the call (A's encoders, the GEMM
+    kernel and the exact kernel queued behind it) is captured in a CUDA graph and each of ``steps``
+    replays is timed with its own events, an L2 flush before each outside them."""
+    import torch
+
+    stream = torch.cuda.current_stream(dev)
+    if flush is None:
+        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    ops = step.operands()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        step.gemm(*ops)
+        step.gemm(*ops)
+    stream.wait_stream(side)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step.gemm(*ops)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    events = []
+    for _ in range(steps):
+        flush.fill_(1)
+        e0, e1 = event_pair()
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        events.append((e0, e1))
+    torch.cuda.synchronize(dev)
+    del graph, ops
     return [a.elapsed_time(b) for a, b in events]
 
 
@@ -761,7 +798,6 @@ def run_b200(args) -> None:
 
     step, macs, _, host_inputs = gemm_step("cfg2", dev, world, rank)
     stream = torch.cuda.current_stream(dev)
-    gemm_events = []
     # The step's public calls captured as CUDA graphs (GraphedStep); two more for the end-to-end
     # pipeline's double-buffered inputs.
     graphed = [GraphedStep("cfg2", dev, world, rank, host_inputs) for _ in range(3)]
@@ -791,19 +827,9 @@ def run_b200(args) -> None:
         if world > 1:
             dist.barrier()
         launches = gstep.launches_per_step * args.steps  # graph replays launch the captured kernels
-        # The GEMM call alone on operands quantized beforehand, with events around it on the stream it
-        # launches on. B's encoding is kept on its operand between calls (as a weight's is), so the
-        # events span A's encoders and the GDFS kernel.
-        ops = step.operands()
-        for _ in range(args.steps):
-            flush.fill_(1)
-            e0, e1 = event_pair()
-            e0.record(stream)
-            step.gemm(*ops)
-            e1.record(stream)
-            gemm_events.append((e0, e1))
-        torch.cuda.synchronize(dev)
-        del ops
+        # The GEMM call alone (A's encoders and the GDFS kernel; B's encoding kept on its operand),
+        # graph-replayed so that the host's work per call does not show between the events.
+        gemm_ms = time_gemm_graphed(step, dev, args.steps, flush)
         # End to end through the public API from pinned host memory.
         pinned = [h.pin_memory() for h in host_inputs]
         t_e2e, h2d, d2h = e2e_pipelined(graphed[1:], pinned, dev, args.steps, args.warmup, world)
@@ -816,7 +842,6 @@ def run_b200(args) -> None:
         # The FP8 CoFDA GEMM (cfg3, 8192^3) split the same way as the headline.
         strong = None if (args.quick and world == 1) else measure_gemm_config(dev, "cfg3", 3, 1, world, rank)
     step_ms = [a.elapsed_time(b) for a, b in step_events]
-    gemm_ms = [a.elapsed_time(b) for a, b in gemm_events]
 
     t_step, t_gemm, t_e2e = max_over_ranks([statistics.mean(step_ms), statistics.mean(gemm_ms), t_e2e], dev, world)
     sizes = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
@@ -894,8 +919,8 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true", help="skip the slow auxiliary measurements (Triton, cfg3)")
-    ap.add_argument("--workload", default="all", choices=["all", "cfg2step", "cfg1", "cfg3", "cfg4", "decode", "triton", "rows",
-                                                      "gdfs_row"],
+    ap.add_argument("--workload", default="all", choices=["all", "cfg2step", "cfg2gemm", "cfg1", "cfg3", "cfg4", "decode",
+                                                      "triton", "rows", "gdfs_row"],
                     help="run only that measurement on one GPU (for profiling)")
     ap.add_argument("--cube", type=int, default=0,
                     help="with --workload cfg3: run an M = N = K = CUBE case instead of 8192 (profiling)")
@@ -910,6 +935,10 @@ def main() -> None:
         torch.cuda.set_device(dev)
         if args.workload == "cfg1":
             print(json.dumps(measure_cfg1(dev, args.steps, args.warmup)))
+        elif args.workload == "cfg2gemm":  # the GEMM call alone, graph-replayed
+            step, macs, shape, _ = gemm_step("cfg2", dev)
+            t = statistics.mean(time_gemm_graphed(step, dev, max(args.steps, 1)))
+            print(json.dumps({"workload": "cfg2 GEMM", "shape": list(shape), "ms": t, "gmacs": macs / (t * 1e-3) / 1e9}))
         elif args.workload == "cfg2step":
             step, macs, shape, _ = gemm_step("cfg2", dev)
             t = statistics.mean(time_steps(step, dev, args.steps, args.warmup))

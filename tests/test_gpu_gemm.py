@@ -470,3 +470,36 @@ def test_gdfs_narrow_kernel_cancelling_groups():
         assert exact_fallbacks() == before
         want = _oracle_gemm(opa, opb, spec)
         assert bits_equal(got, want), f"k_tile={kt}: {first_mismatch(got, want)}"
+
+
+def test_gdfs_narrow_kernel_wide_label_spread():
+    """Groups whose products span more than G - ma - mb binades truncate their smallest products at
+    radix G, so the kernel's exact-sum shortcut must not take them: rows and columns mixing the
+    largest E4M3 magnitudes with subnormals (labels 8 and -9 on each side), next to ordinary rows in
+    the same warps, bit for bit with the oracle for G = 32 (span 26) and G = 20 (span 14)."""
+    g = torch.Generator().manual_seed(11)
+
+    def fp8(x):
+        return x.to(torch.float8_e4m3fn).float()
+
+    m, n, k = 40, 48, 128
+    a = fp8(torch.randn(m, k, generator=g) * 2)
+    b = fp8(torch.randn(n, k, generator=g) * 2)
+    for r in range(0, m, 5):
+        a[r, r % 16::16] = 448.0
+        a[r, (r + 3) % 16::16] = 2.0 ** -9
+    for c in range(0, n, 7):
+        b[c, (c + 1) % 16::16] = -448.0
+        b[c, (c + 5) % 16::16] = 2.0 ** -8
+    from tricast_b200.formats import FP32, get_format
+
+    one = torch.ones((), device="cuda")
+    opa = Operand(a.cuda(), get_format("fp8_e4m3"), one, FP32, "tensor")
+    opb = Operand(b.cuda(), get_format("fp8_e4m3"), one, FP32, "tensor")
+    for g_bits in (32, 20):
+        spec = MMASpec("gdfs", f_bits=25, g_bits=g_bits, group_size=16, k_tile=32, out_format="fp32")
+        before = exact_fallbacks()
+        got = gemm_triton(opa, opb, spec).cpu().numpy()
+        assert exact_fallbacks() == before
+        want = _oracle_gemm(opa, opb, spec)
+        assert bits_equal(got, want), f"g_bits={g_bits}: {first_mismatch(got, want)}"

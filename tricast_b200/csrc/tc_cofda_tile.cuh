@@ -28,6 +28,7 @@ struct EncodeArgs {
   int field0;
   void *val;           // [tile][chunk][k][kTile], float or double
   uint32_t *exp;       // A: [tile][chunk][k][kTile/2] (pairs of rows); B: [tile][chunk][k][kTile] (duplicated)
+  void *sgn;           // optional, laid out as val: val then holds |value| and sgn its sign as +-1
   int side;
   int32_t *flag;
 };
@@ -77,6 +78,12 @@ __global__ void __launch_bounds__(256) encode_kernel(EncodeArgs e) {
       exps[h] = ex;
     }
     const int64_t base = ((tile * e.nchunks + chunk) * e.CS + kk) * kTile;
+    if (e.sgn) {
+      static_cast<T *>(e.sgn)[base + rp * 2] = signbit(vals[0]) ? (T)-1 : (T)1;
+      static_cast<T *>(e.sgn)[base + rp * 2 + 1] = signbit(vals[1]) ? (T)-1 : (T)1;
+      vals[0] = fabsf(vals[0]);
+      vals[1] = fabsf(vals[1]);
+    }
     static_cast<T *>(e.val)[base + rp * 2] = (T)vals[0];
     static_cast<T *>(e.val)[base + rp * 2 + 1] = (T)vals[1];
     if (e.side == 0) {

@@ -24,6 +24,15 @@
 // product; a group whose aligned sum cancels to exactly zero takes no part in the reference's FDA, so
 // an output where that changes emax_t redoes its tile step with the true emax_t (rare).
 //
+// No truncation: a non-zero product is sig * 2**(e_k - ma - mb) with an integer significand product
+// (ma, mb the operands' mantissa bits), so floor(|P_k| * 2**(G - emax_g)) drops nothing when
+// emax_g - e_k <= G - ma - mb. A thread checks that bound for each of its outputs and groups from the
+// group's largest product label and the smallest non-zero labels of its rows and columns (kept per
+// (row, group) by min_label_kernel); when all 32 lanes pass, the group's sum is the exact fp64 sum of
+// its products (one FMA each: at most G + 2 + log2 GS <= 53 significant bits), and its tile term
+// floor(|sum| * 2**(F - emax_t)) is the same as that of the aligned sum. Otherwise every product is
+// truncated as above.
+//
 // Operands are staged as the CoFDA kernel's are (tc_cofda_tile.cuh) with one chunk per group: values
 // in fp64 and packed int16 labels, power-of-two K scales constant over a group folded in at encode
 // time (equal to GDFS's group-level exponent add). Anything else goes to the exact generic kernel.
@@ -40,6 +49,40 @@ using cofda::kTile;
 using cofda::kZeroExp;
 using cofda::load4;
 
+constexpr int kNoLabel = 0x7FFF;  // smallest label of a row or column with no non-zero element
+
+// One group's stage: the tile layout's values and labels, plus each row's and column's smallest
+// non-zero label in the group.
+template <int GS>
+struct GStage {
+  double av[GS][kTile];
+  double bv[GS][kTile];
+  uint32_t be[GS][kTile];
+  uint32_t ae[GS][kTile / 2];
+  int16_t amin[kTile];
+  int16_t bmin[kTile];
+};
+
+// Per (row tile, chunk, row): the smallest label among the row's non-zero elements of the chunk
+// (kNoLabel when it has none), from the encoded labels (A: row pairs, B: duplicated halves).
+__global__ void __launch_bounds__(256) min_label_kernel(const uint32_t *__restrict__ exp, int side, int64_t rows_pad,
+                                                        int64_t nchunks, int CS, int16_t *__restrict__ out) {
+  const int64_t total = rows_pad * nchunks;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(idx % kTile);
+    const int64_t tc = idx / kTile;  // row tile * nchunks + chunk
+    int mn = kNoLabel;
+    for (int kk = 0; kk < CS; ++kk) {
+      const int64_t base = (tc * CS + kk) * kTile;
+      const uint32_t w = side == 0 ? exp[base / 2 + r / 2] >> ((r & 1) * 16) : exp[base + r];
+      const int lab = (int)(int16_t)(w & 0xFFFFu);
+      if (lab != kZeroExp) mn = min(mn, lab);
+    }
+    out[idx] = (int16_t)mn;
+  }
+}
+
 // Output (i, j)'s label from the packed pair of rows (2q, 2q + 1) of pass 1. A product with a zero
 // element carries kZeroExp plus the other element's label (at most a few hundred above kZeroExp,
 // far below any real label): a group with no non-zero product reads as kZeroExp.
@@ -53,14 +96,14 @@ __device__ __forceinline__ int emax_of(const uint32_t (&e)[2][4], int i, int j) 
 // to zero had set it): every group's sum recomputed from the staged operands, only the non-zero ones
 // and the running value taking part. Rare, so kept out of line.
 template <int GS, int NG, bool RNE>
-__device__ __noinline__ float redo_tile(const cofda::Stage<GS, double> *stages, int64_t c0, int i, int j, int tx, int ty,
+__device__ __noinline__ float redo_tile(const GStage<GS> *stages, int64_t c0, int i, int j, int tx, int ty,
                                         float c, int4 egs, int F, int G) {
   constexpr int kSt = 2 * NG;
   const int egv[4] = {egs.x, egs.y, egs.z, egs.w};
   double sums[NG];
   int et = cofda::running_exp(c);
   for (int gg = 0; gg < NG; ++gg) {
-    const cofda::Stage<GS, double> &st = stages[(c0 + gg) % kSt];
+    const GStage<GS> &st = stages[(c0 + gg) % kSt];
     const int eg = egv[gg];
     const double S = Acc<double>::pow2(G - eg);
     double sum = 0.0;
@@ -79,8 +122,9 @@ __device__ __noinline__ float redo_tile(const cofda::Stage<GS, double> *stages, 
 struct Args {
   const double *av, *bv;
   const uint32_t *ae, *be;
+  const int16_t *amin, *bmin;  // [tile][chunk][kTile]: smallest non-zero label per row / column
   int64_t M, N, ntiles;
-  int F, G;
+  int F, G, span;              // span = G - ma - mb: the label distance below emax_g kept exactly
   GemmDesc g;
   const int32_t *flag;
   int32_t *status;
@@ -91,7 +135,7 @@ template <int GS, int NG, bool RNE>
 __global__ void __launch_bounds__(256) gdfs_kernel(Args p) {
   if (*p.flag) return;
   constexpr int kSt = 2 * NG;  // the stages of two K tiles: one being scanned, one in flight
-  using Stage = cofda::Stage<GS, double>;
+  using Stage = GStage<GS>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   Stage *stages = reinterpret_cast<Stage *>(smem_raw);
   __shared__ __align__(8) uint64_t full[kSt];
@@ -101,7 +145,8 @@ __global__ void __launch_bounds__(256) gdfs_kernel(Args p) {
   constexpr uint32_t kValBytes = GS * kTile * 8;
   constexpr uint32_t kBexpBytes = GS * kTile * 4;
   constexpr uint32_t kAexpBytes = GS * (kTile / 2) * 4;
-  constexpr uint32_t kStageBytes = 2 * kValBytes + kBexpBytes + kAexpBytes;
+  constexpr uint32_t kMinBytes = kTile * 2;
+  constexpr uint32_t kStageBytes = 2 * kValBytes + kBexpBytes + kAexpBytes + 2 * kMinBytes;
   const int64_t nchunks = p.ntiles * NG;
 
   if (threadIdx.x == 0) {
@@ -119,6 +164,8 @@ __global__ void __launch_bounds__(256) gdfs_kernel(Args p) {
     bulk_g2s(&st.ae[0][0], p.ae + a_off / 2, kAexpBytes, &full[s]);
     bulk_g2s(&st.bv[0][0], p.bv + b_off, kValBytes, &full[s]);
     bulk_g2s(&st.be[0][0], p.be + b_off, kBexpBytes, &full[s]);
+    bulk_g2s(&st.amin[0], p.amin + (mt * nchunks + c) * kTile, kMinBytes, &full[s]);
+    bulk_g2s(&st.bmin[0], p.bmin + (nt * nchunks + c) * kTile, kMinBytes, &full[s]);
   };
   if (threadIdx.x == 0)
     for (int64_t c = 0; c < kSt && c < nchunks; ++c) issue(c);
@@ -189,33 +236,73 @@ __global__ void __launch_bounds__(256) gdfs_kernel(Args p) {
 #pragma unroll
     for (int gg = 0; gg < NG; ++gg) {
       const Stage &st = stages[(c0 + gg) % kSt];
-      double S[4][4], sum[4][4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          S[i][j] = Acc<double>::pow2(G - emax_of(em2[gg], i, j));
-          sum[i][j] = 0.0;
-        }
-#pragma unroll 4
-      for (int kk = 0; kk < GS; ++kk) {
-        double as[4], bs[4];
-        load4<double>(&st.av[kk][ty * 4], as);
-        load4<double>(&st.bv[kk][tx * 4], bs);
+      double sum[4][4];
+      bool exact = true;  // no product of this thread's outputs is truncated at radix G
+      {
+        const uint2 am = *reinterpret_cast<const uint2 *>(&st.amin[ty * 4]);
+        const uint2 bm = *reinterpret_cast<const uint2 *>(&st.bmin[tx * 4]);
+        const int ra[4] = {(int)(int16_t)(am.x & 0xFFFFu), (int)(int16_t)(am.x >> 16), (int)(int16_t)(am.y & 0xFFFFu),
+                           (int)(int16_t)(am.y >> 16)};
+        const int cb[4] = {(int)(int16_t)(bm.x & 0xFFFFu), (int)(int16_t)(bm.x >> 16), (int)(int16_t)(bm.y & 0xFFFFu),
+                           (int)(int16_t)(bm.y >> 16)};
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            sum[i][j] = __dadd_rn(sum[i][j], Acc<double>::trunc(__dmul_rn(as[i], bs[j]), S[i][j]));
+          for (int j = 0; j < 4; ++j) exact &= emax_of(em2[gg], i, j) - ra[i] - cb[j] <= p.span;
       }
+      if (__all_sync(0xFFFFFFFFu, exact)) {
+        // The exact sum of the products: the aligned sum at radix G times 2**(emax_g - G).
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int eg = emax_of(em2[gg], i, j);
-          total[i][j] = __dadd_rn(total[i][j], Acc<double>::trunc(sum[i][j], Acc<double>::pow2(F - G + eg - et[i][j])));
-          live[i][j] = sum[i][j] != 0.0 ? max(live[i][j], eg) : live[i][j];
+          for (int j = 0; j < 4; ++j) sum[i][j] = 0.0;
+#pragma unroll 4
+        for (int kk = 0; kk < GS; ++kk) {
+          double as[4], bs[4];
+          load4<double>(&st.av[kk][ty * 4], as);
+          load4<double>(&st.bv[kk][tx * 4], bs);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sum[i][j] = __fma_rn(as[i], bs[j], sum[i][j]);
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int eg = emax_of(em2[gg], i, j);
+            total[i][j] = __dadd_rn(total[i][j], Acc<double>::trunc(sum[i][j], Acc<double>::pow2(F - et[i][j])));
+            live[i][j] = sum[i][j] != 0.0 ? max(live[i][j], eg) : live[i][j];
+          }
+      } else {
+        double S[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            S[i][j] = Acc<double>::pow2(G - emax_of(em2[gg], i, j));
+            sum[i][j] = 0.0;
+          }
+#pragma unroll 4
+        for (int kk = 0; kk < GS; ++kk) {
+          double as[4], bs[4];
+          load4<double>(&st.av[kk][ty * 4], as);
+          load4<double>(&st.bv[kk][tx * 4], bs);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              sum[i][j] = __dadd_rn(sum[i][j], Acc<double>::trunc(__dmul_rn(as[i], bs[j]), S[i][j]));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int eg = emax_of(em2[gg], i, j);
+            total[i][j] = __dadd_rn(total[i][j], Acc<double>::trunc(sum[i][j], Acc<double>::pow2(F - G + eg - et[i][j])));
+            live[i][j] = sum[i][j] != 0.0 ? max(live[i][j], eg) : live[i][j];
+          }
+      }
     }
     // Normalise; an output whose tile exponent came only from groups that cancelled to zero redoes
     // its step with the true exponent. An overflowed running value is sticky (operands are finite).
@@ -268,7 +355,7 @@ struct GdfsPlan {
   bool ok;
   int GS, NG;
   int64_t ntiles, a_pad, b_pad;
-  size_t off[4], flag_off, total;
+  size_t off[6], flag_off, total;  // A values, A labels, B values, B labels, A / B smallest labels
 };
 
 static int bit_length(int64_t v) {
@@ -286,7 +373,7 @@ static GdfsPlan plan_gdfs(const GemmDesc &g) {
   if (g.KT % g.GS) return p;
   const int ng = g.KT / g.GS;
   if (ng != 1 && ng != 2 && ng != 4) return p;
-  if ((size_t)2 * ng * sizeof(cofda::Stage<32, double>) * g.GS / 32 > 200 * 1024) return p;
+  if ((size_t)2 * ng * (sizeof(gdfs::GStage<32>) * g.GS / 32 + 256) > 200 * 1024) return p;
   if (g.G < 1 || g.G + 2 + bit_length(g.GS) > 53) return p;           // exact group sums in fp64
   if (g.F < 1 || g.F + 3 + bit_length(ng * g.GS) > 53) return p;      // exact tile totals in fp64
   if (g.apply == AP_GROUP) {
@@ -304,9 +391,9 @@ static GdfsPlan plan_gdfs(const GemmDesc &g) {
   p.b_pad = (g.N + kTile - 1) / kTile * kTile;
   const int64_t nchunks = p.ntiles * ng;
   const size_t ka = (size_t)p.a_pad * nchunks * g.GS, kb = (size_t)p.b_pad * nchunks * g.GS;
-  const size_t sizes[4] = {ka * 8, ka * 2, kb * 8, kb * 4};
+  const size_t sizes[6] = {ka * 8, ka * 2, kb * 8, kb * 4, (size_t)p.a_pad * nchunks * 2, (size_t)p.b_pad * nchunks * 2};
   size_t off = 0;
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < 6; ++i) {
     p.off[i] = off;
     off += (sizes[i] + 255) & ~(size_t)255;
   }
@@ -323,7 +410,7 @@ size_t gdfs_workspace(const GemmDesc &g) {
 
 template <int GS, int NG, bool RNE>
 static int launch_gdfs_kernel(const gdfs::Args &a, cudaStream_t s) {
-  const size_t smem = sizeof(cofda::Stage<GS, double>) * 2 * NG;
+  const size_t smem = sizeof(gdfs::GStage<GS>) * 2 * NG;
   cudaError_t e = cudaFuncSetAttribute(gdfs::gdfs_kernel<GS, NG, RNE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return set_error(std::string("gdfs: ") + cudaGetErrorString(e)), TC_CUDA_ERROR;
@@ -381,6 +468,11 @@ int launch_gdfs(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
     const int64_t blocks = std::min<int64_t>((work + 255) / 256, (int64_t)sm_count() * 16);
     cofda::encode_kernel<double><<<(unsigned)blocks, 256, 0, s>>>(e);
     count_launch();
+    const int64_t rows = e.rows_pad * nchunks;
+    const int64_t mblocks = std::min<int64_t>((rows + 255) / 256, (int64_t)sm_count() * 16);
+    gdfs::min_label_kernel<<<(unsigned)mblocks, 256, 0, s>>>(e.exp, side, e.rows_pad, nchunks, p.GS,
+                                                             reinterpret_cast<int16_t *>(ws + p.off[4 + side]));
+    count_launch();
   }
   gdfs::Args a;
   std::memset(&a, 0, sizeof(a));
@@ -388,11 +480,14 @@ int launch_gdfs(const GemmDesc &g, void *workspace, size_t workspace_bytes, cuda
   a.ae = reinterpret_cast<const uint32_t *>(ws + p.off[1]);
   a.bv = reinterpret_cast<const double *>(ws + p.off[2]);
   a.be = reinterpret_cast<const uint32_t *>(ws + p.off[3]);
+  a.amin = reinterpret_cast<const int16_t *>(ws + p.off[4]);
+  a.bmin = reinterpret_cast<const int16_t *>(ws + p.off[5]);
   a.M = g.M;
   a.N = g.N;
   a.ntiles = p.ntiles;
   a.F = g.F;
   a.G = g.G;
+  a.span = g.G - g.a.f.mbits - g.b.f.mbits;
   a.g = g;
   a.flag = flag;
   a.status = flag + 1;
