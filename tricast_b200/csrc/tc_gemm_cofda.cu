@@ -67,7 +67,7 @@ struct Args {
 };
 
 template <int CS, bool RNE, class T>
-__global__ void __launch_bounds__(256) cofda_kernel(Args p) {
+__global__ void __launch_bounds__(256, sizeof(T) == 4 ? 2 : 1) cofda_kernel(Args p) {
   if (*p.flag) return;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   SStage<CS, T> *stages = reinterpret_cast<SStage<CS, T> *>(smem_raw);
@@ -106,6 +106,7 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
     for (int j = 0; j < 4; ++j) c[i][j] = acc[i][j] = 0.0f;
 
   const int F = p.F;
+  constexpr uint32_t kZeroPair = ((uint32_t)kZeroExp & 0xFFFFu) | ((uint32_t)kZeroExp << 16);
   bool timed_out = false;
   for (int64_t ch = 0; ch < p.nchunks; ++ch) {
     const int s = (int)(ch % kStages);
@@ -125,7 +126,7 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
     for (int q = 0; q < 2; ++q)
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        em2[q][j] = p.dec ? (((uint32_t)kZeroExp & 0xFFFFu) | ((uint32_t)kZeroExp << 16))  // decoupled: c not in the chunk
+        em2[q][j] = p.dec ? kZeroPair  // decoupled: c takes no part in the chunk
                           : ((uint32_t)running_exp(c[2 * q][j]) & 0xFFFFu) | ((uint32_t)running_exp(c[2 * q + 1][j]) << 16);
 #pragma unroll 8
     for (int kk = 0; kk < CS; ++kk) {
@@ -138,11 +139,9 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
         em2[1][j] = __viaddmax_s16x2(ea.y, ebs[j], em2[1][j]);
       }
     }
-    // The per-output steps of the chunk. With fp64 accumulation they run as selects plus a redo of
-    // the rare outputs (blackwell_fp8 at 4096^3: 41.0 -> 35.6 ms against per-output branches); with
-    // fp32 the per-output branches stay, which measured faster than selects there (hopper_fp8: 18.9
-    // vs 20.9 ms once the decoupled-mode test is outside the loop).
-    constexpr bool kSelect = sizeof(T) == 8;
+    // The per-output steps of the chunk run as selects plus a redo of the rare outputs (blackwell_fp8
+    // at 4096^3: 41.0 -> 35.6 ms against per-output branches; hopper_fp8 at 8192^3: 144.9 -> 135.8 ms,
+    // with the fp32 kernel held to 128 registers so that two CTAs stay resident per SM).
     int emax[4][4];
     T S[4][4], tot[4][4];
     uint32_t rare = 0;  // outputs whose running value needs the integer alignment (F - emax > 127)
@@ -153,16 +152,12 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
         const uint32_t w = em2[i >> 1][j];
         emax[i][j] = (int)(int16_t)((i & 1) ? (w >> 16) : (w & 0xFFFFu));
         S[i][j] = Acc<T>::pow2(F - emax[i][j]);
-        if constexpr (kSelect) {
-          bool rr;
-          const T t0 = Acc<T>::running_fast(c[i][j], S[i][j], F, emax[i][j], rr);
-          tot[i][j] = p.dec ? (T)0 : t0;
-          rare |= (uint32_t)(rr && !p.dec) << (i * 4 + j);
-        } else {
-          tot[i][j] = p.dec ? (T)0 : Acc<T>::running(c[i][j], F, emax[i][j], S[i][j]);
-        }
+        bool rr;
+        const T t0 = Acc<T>::running_fast(c[i][j], S[i][j], F, emax[i][j], rr);
+        tot[i][j] = p.dec ? (T)0 : t0;
+        rare |= (uint32_t)(rr && !p.dec) << (i * 4 + j);
       }
-    if (kSelect && rare) {
+    if (rare) {
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -190,15 +185,6 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           c[i][j] = merge_decoupled(Acc<T>::finish(tot[i][j], emax[i][j], F, RNE), c[i][j], p.F2, RNE);
-    } else if constexpr (!kSelect) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t cb = f2u(c[i][j]) & 0x7FFFFFFFu;
-          const float r = Acc<T>::finish(tot[i][j], emax[i][j], F, RNE);
-          if (cb < kInf) c[i][j] = r;  // an overflowed running value is sticky (operands are finite)
-        }
     } else {
       // Normalise with selects; outputs outside the normal range (rare) are redone by the general
       // routine. An overflowed running value is sticky (operands are finite).
@@ -239,6 +225,7 @@ __global__ void __launch_bounds__(256) cofda_kernel(Args p) {
           acc[i][j] = __fmaf_rn(c[i][j], w, acc[i][j]);
           c[i][j] = 0.0f;
         }
+
     }
     __syncthreads();
     if (threadIdx.x == 0 && ch + kStages < p.nchunks) issue(ch + kStages, s);
