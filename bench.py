@@ -727,6 +727,53 @@ def run_reference(args) -> None:
 
 
 # ------------------------------------------------------------------------------------ end to end
+def gpu_local_cpus(dev) -> set | None:
+    """The host CPUs local to the GPU's PCI device (sysfs ``local_cpulist``) that this process may
+    use, or None where sysfs does not say."""
+    import torch
+
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        bdf = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        text = open(f"/sys/bus/pci/devices/{bdf}/local_cpulist").read().strip()
+    except (OSError, AttributeError, ValueError):
+        return None
+    cpus = set()
+    for part in text.split(","):
+        if "-" in part:
+            lo, hi = part.split("-")
+            cpus.update(range(int(lo), int(hi) + 1))
+        elif part:
+            cpus.add(int(part))
+    cpus &= os.sched_getaffinity(0)
+    return cpus or None
+
+
+def copy_bandwidth(host_inputs, out, dev) -> dict:
+    """One host -> device copy of the step's inputs and one device -> host copy of its output, each
+    timed with events on a side stream (GB/s): the link the end-to-end number rides on."""
+    import torch
+
+    side = torch.cuda.Stream(dev)
+    dst = [torch.empty_like(h, device=dev) for h in host_inputs]
+    back = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    res = {}
+    with torch.cuda.stream(side):
+        for name, fn, nbytes in (("h2d_gbs", lambda: [d.copy_(h, non_blocking=True) for d, h in zip(dst, host_inputs)],
+                                  sum(h.numel() * h.element_size() for h in host_inputs)),
+                                 ("d2h_gbs", lambda: back.copy_(out, non_blocking=True),
+                                  out.numel() * out.element_size())):
+            fn()
+            e0, e1 = event_pair()
+            e0.record(side)
+            fn()
+            e1.record(side)
+            e1.synchronize()
+            res[name] = nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    torch.cuda.synchronize(dev)
+    return res
+
+
 def e2e_pipelined(steppers, host_inputs, dev, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
     """The step end to end from pinned host memory, as a serving loop runs it: every step copies its
     inputs host -> device (a copy stream), runs the step (the compute stream) and copies its result
@@ -830,9 +877,20 @@ def run_b200(args) -> None:
         # The GEMM call alone (A's encoders and the GDFS kernel; B's encoding kept on its operand),
         # graph-replayed so that the host's work per call does not show between the events.
         gemm_ms = time_gemm_graphed(step, dev, args.steps, flush)
-        # End to end through the public API from pinned host memory.
-        pinned = [h.pin_memory() for h in host_inputs]
-        t_e2e, h2d, d2h = e2e_pipelined(graphed[1:], pinned, dev, args.steps, args.warmup, world)
+        # End to end through the public API from pinned host memory. The host buffers are pinned by a
+        # thread held to the GPU's local CPUs (their pages land on its NUMA node), as a serving
+        # process bound to its GPU would hold them; the process's affinity is restored afterwards.
+        affinity = os.sched_getaffinity(0)
+        local_cpus = gpu_local_cpus(dev)
+        if local_cpus:
+            os.sched_setaffinity(0, local_cpus)
+        try:
+            pinned = [h.pin_memory() for h in host_inputs]
+            links = copy_bandwidth(pinned, graphed[1].out, dev)
+            t_e2e, h2d, d2h = e2e_pipelined(graphed[1:], pinned, dev, args.steps, args.warmup, world)
+        finally:
+            os.sched_setaffinity(0, affinity)
+        links["host_cpus"] = "gpu-local NUMA node" if local_cpus else "process default (no sysfs locality)"
         # Layer sweep (cfg5): per-shape costs measured at full size (which also warms every shape
         # up), LPT on them, then the device-timed sweep, max over ranks.
         cfg = SweepConfig()
@@ -869,7 +927,8 @@ def run_b200(args) -> None:
                     "d2h_bytes_per_step": d2h_all,
                     "protocol": "K steps pipelined from pinned host memory: upload, compute and download on three "
                                 "streams with double-buffered inputs and outputs; timed from the first upload to "
-                                "the last download; bytes summed over ranks"},
+                                "the last download; bytes summed over ranks",
+                    "links_rank0": {k: (round(v, 1) if isinstance(v, float) else v) for k, v in links.items()}},
             "gpu_launches": int(launches),
             "graphs": "each step replays CUDA graphs of its public calls; gpu_launches = the library kernels "
                       "one step launches (counted on an eager step) x steps",
