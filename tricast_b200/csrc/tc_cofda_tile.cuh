@@ -33,6 +33,27 @@ struct EncodeArgs {
   int32_t *flag;
 };
 
+// Position of column c of a 64-wide tile among the staged B values. fp32 keeps the natural order (a
+// thread's four columns are one 16-byte load, 16 threads read 256 contiguous bytes); fp64 puts columns
+// 4t, 4t + 1 at 2t, 2t + 1 and 4t + 2, 4t + 3 at 32 + 2t, 33 + 2t, so each of a thread's two 16-byte
+// loads is again one of 16 contiguous pairs (no shared-memory bank conflicts).
+template <class T>
+__host__ __device__ __forceinline__ int bcol(int c) {
+  return sizeof(T) == 8 ? ((c & 2) << 4) + ((c >> 2) << 1) + (c & 1) : c;
+}
+
+// Thread tx's four B values (columns 4 tx .. 4 tx + 3) of one k from the staged row.
+template <class T>
+__device__ __forceinline__ void load_b4(const T *row, int tx, T (&o)[4]) {
+  if constexpr (sizeof(T) == 4) {
+    load4<T>(row + tx * 4, o);
+  } else {
+    const double2 v0 = *reinterpret_cast<const double2 *>(row + tx * 2);
+    const double2 v1 = *reinterpret_cast<const double2 *>(row + 32 + tx * 2);
+    o[0] = v0.x; o[1] = v0.y; o[2] = v1.x; o[3] = v1.y;
+  }
+}
+
 template <class T>
 __global__ void __launch_bounds__(256) encode_kernel(EncodeArgs e) {
   const int64_t pairs = e.rows_pad / 2;
@@ -84,8 +105,10 @@ __global__ void __launch_bounds__(256) encode_kernel(EncodeArgs e) {
       vals[0] = fabsf(vals[0]);
       vals[1] = fabsf(vals[1]);
     }
-    static_cast<T *>(e.val)[base + rp * 2] = (T)vals[0];
-    static_cast<T *>(e.val)[base + rp * 2 + 1] = (T)vals[1];
+    const int c0 = e.side ? bcol<T>((int)rp * 2) : (int)rp * 2;  // B: the loads' column order
+    const int c1 = e.side ? bcol<T>((int)rp * 2 + 1) : (int)rp * 2 + 1;
+    static_cast<T *>(e.val)[base + c0] = (T)vals[0];
+    static_cast<T *>(e.val)[base + c1] = (T)vals[1];
     if (e.side == 0) {
       e.exp[base / 2 + rp] = ((uint32_t)exps[0] & 0xFFFFu) | ((uint32_t)exps[1] << 16);
     } else {

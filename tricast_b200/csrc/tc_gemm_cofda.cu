@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 4 ? 2 : 1) cofda_kernel(Args
       T am[4], sg[4], bs[4], mb[4];
       load4<T>(&st.av[kk][ty * 4], am);
       load4<T>(&st.as[kk][ty * 4], sg);
-      load4<T>(&st.bv[kk][tx * 4], bs);
+      load_b4<T>(&st.bv[kk][0], tx, bs);
 #pragma unroll
       for (int j = 0; j < 4; ++j) mb[j] = Acc<T>::magic(bs[j]);
 #pragma unroll

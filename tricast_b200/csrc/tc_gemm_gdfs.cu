@@ -108,7 +108,7 @@ __device__ __noinline__ float redo_tile(const GStage<GS> *stages, int64_t c0, in
     const double S = Acc<double>::pow2(G - eg);
     double sum = 0.0;
     for (int kk = 0; kk < GS; ++kk)
-      sum = __dadd_rn(sum, Acc<double>::trunc(__dmul_rn(st.av[kk][ty * 4 + i], st.bv[kk][tx * 4 + j]), S));
+      sum = __dadd_rn(sum, Acc<double>::trunc(__dmul_rn(st.av[kk][ty * 4 + i], st.bv[kk][cofda::bcol<double>(tx * 4 + j)]), S));
     sums[gg] = sum;
     if (sum != 0.0) et = max(et, eg);
   }
@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(256) gdfs_kernel(Args p) {
         for (int kk = 0; kk < GS; ++kk) {
           double as[4], bs[4];
           load4<double>(&st.av[kk][ty * 4], as);
-          load4<double>(&st.bv[kk][tx * 4], bs);
+          cofda::load_b4<double>(&st.bv[kk][0], tx, bs);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(256) gdfs_kernel(Args p) {
         for (int kk = 0; kk < GS; ++kk) {
           double as[4], bs[4];
           load4<double>(&st.av[kk][ty * 4], as);
-          load4<double>(&st.bv[kk][tx * 4], bs);
+          cofda::load_b4<double>(&st.bv[kk][0], tx, bs);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
 #pragma unroll
