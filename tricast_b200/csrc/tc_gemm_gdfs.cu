@@ -225,13 +225,15 @@ __global__ void __launch_bounds__(256) gdfs_kernel(Args p) {
       }
     // Pass 2: each group's exact aligned sum at radix G, folded into the tile total at radix F.
     double total[4][4];
-    int live[4][4];  // the largest exponent of a group whose sum is non-zero
+    // Bit i * 4 + j: output (i, j)'s tile exponent is attained by a term that takes part (its running
+    // value, or a group whose sum is non-zero); otherwise the true exponent is smaller (a redo).
+    uint32_t held = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         total[i][j] = Acc<double>::running(c[i][j], F, et[i][j], Acc<double>::pow2(F - et[i][j]));
-        live[i][j] = kZeroExp;
+        held |= (uint32_t)(cofda::running_exp(c[i][j]) == et[i][j]) << (i * 4 + j);
       }
 #pragma unroll
     for (int gg = 0; gg < NG; ++gg) {
@@ -272,7 +274,7 @@ __global__ void __launch_bounds__(256) gdfs_kernel(Args p) {
           for (int j = 0; j < 4; ++j) {
             const int eg = emax_of(em2[gg], i, j);
             total[i][j] = __dadd_rn(total[i][j], Acc<double>::trunc(sum[i][j], Acc<double>::pow2(F - et[i][j])));
-            live[i][j] = sum[i][j] != 0.0 ? max(live[i][j], eg) : live[i][j];
+            held |= (uint32_t)((sum[i][j] != 0.0) & (eg == et[i][j])) << (i * 4 + j);
           }
       } else {
         double S[4][4];
@@ -300,7 +302,7 @@ __global__ void __launch_bounds__(256) gdfs_kernel(Args p) {
           for (int j = 0; j < 4; ++j) {
             const int eg = emax_of(em2[gg], i, j);
             total[i][j] = __dadd_rn(total[i][j], Acc<double>::trunc(sum[i][j], Acc<double>::pow2(F - G + eg - et[i][j])));
-            live[i][j] = sum[i][j] != 0.0 ? max(live[i][j], eg) : live[i][j];
+            held |= (uint32_t)((sum[i][j] != 0.0) & (eg == et[i][j])) << (i * 4 + j);
           }
       }
     }
@@ -311,10 +313,10 @@ __global__ void __launch_bounds__(256) gdfs_kernel(Args p) {
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int true_et = max(cofda::running_exp(c[i][j]), live[i][j]);
+        const bool same_et = (held >> (i * 4 + j)) & 1u;
         const bool sticky = (f2u(c[i][j]) & 0x7FFFFFFFu) >= kInf;
-        redo |= (uint32_t)(true_et != et[i][j] && !sticky) << (i * 4 + j);
-        if (!sticky && true_et == et[i][j] && et[i][j] != kZeroExp)
+        redo |= (uint32_t)(!same_et && !sticky) << (i * 4 + j);
+        if (!sticky && same_et && et[i][j] != kZeroExp)
           c[i][j] = Acc<double>::finish(total[i][j], et[i][j], F, RNE);
       }
     if (redo) {

@@ -1083,7 +1083,9 @@ extern "C" int tc_quantize(const void *x, int32_t x_dtype, int64_t rows, int64_t
       const int64_t main_groups = rest_groups / per_warp * per_warp;
       if (main_groups > 0) {
         const LeanArgs r = shifted(done, main_groups * gs);
-        const int grid = grid_for(main_groups * lanes_per_group, 256, 8);
+        // Up to 16 CTAs per SM (two resident waves): the cfg1 cast measured 4.585 TB/s against 4.54 with
+        // one wave of 8, 4.41 with 4 and 4.32 with 32.
+        const int grid = grid_for(main_groups * lanes_per_group, 256, 16);
         const int gi = gs == 8 ? 0 : gs == 16 ? 1 : gs == 32 ? 2 : gs == 64 ? 3 : 4;
         if (!out->codes) launch_group_lean_c0(r, grid, gi, pow2, fast, outs, s);
         else if (p.code_bits == 4) launch_group_lean_c4(r, grid, gi, pow2, fast, outs, s);
