@@ -503,3 +503,28 @@ def test_gdfs_narrow_kernel_wide_label_spread():
         assert exact_fallbacks() == before
         want = _oracle_gemm(opa, opb, spec)
         assert bits_equal(got, want), f"g_bits={g_bits}: {first_mismatch(got, want)}"
+
+
+@pytest.mark.parametrize("m,n,k", [(3, 2, 0), (40, 70, 0), (0, 6, 64), (5, 0, 64)])
+@pytest.mark.parametrize("fmt,spec", [
+    ("fp8_e4m3", MMASpec("cofda", f_bits=13, chunk_size=32, out_format="fp32")),
+    ("fp8_e4m3", MMASpec("gdfs", f_bits=25, g_bits=32, group_size=16, k_tile=32, out_format="fp32")),
+    ("fp4_e2m1", MMASpec("gdfs", f_bits=35, g_bits=6, group_size=16, k_tile=64, out_format="bf16")),
+    ("fp8_e4m3", MMASpec("fp64", out_format="fp32")),
+    ("fp8_e4m3", MMASpec("fp32_fma", out_format="fp32")),
+    ("int8", MMASpec("int_exact", out_format="fp32")),
+], ids=lambda x: getattr(x, "algorithm", x))
+def test_empty_shapes(m, n, k, fmt, spec):
+    """Empty products as TriCast's reference treats them: no rows or columns give an empty output, and
+    K = 0 gives each output the epilogue of a zero sum (the bias here)."""
+    from tricast_b200.formats import FP32, get_format
+
+    f = get_format(fmt)
+    one = torch.ones((), device="cuda")
+    a = Operand(torch.zeros(m, k, device="cuda"), f, one, FP32, "tensor")
+    b = Operand(torch.zeros(n, k, device="cuda"), f, one, FP32, "tensor")
+    bias = torch.linspace(-2, 3, n, device="cuda") if n else None
+    got = gemm_triton(a, b, spec, bias=bias)
+    assert tuple(got.shape) == (m, n)
+    want = oracle.gemm_reference(a, b, spec, bias=bias)
+    assert bits_equal(got.float().cpu().numpy(), np.asarray(want).reshape(m, n))

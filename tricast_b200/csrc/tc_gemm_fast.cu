@@ -505,6 +505,7 @@ int launch_fp4_gemv(const GemmDesc &g, int ng, void *workspace, size_t workspace
 constexpr int64_t kGemvMaxM = 16;
 
 size_t fast_workspace(const GemmDesc &g) {
+  if (g.K == 0) return 0;  // no products: the generic kernel writes the epilogue of a zero sum
   Fp4Plan p = plan_fp4(g);
   if (p.ok) return g.M <= kGemvMaxM ? fp4_gemv_workspace(g, p.ng) : p.total;
   size_t w = int_workspace(g);
@@ -595,6 +596,7 @@ static bool fp4_tiled_encodable(const GemmDesc &g, const Fp4Plan &p) {
 }
 
 size_t encoded_b_bytes(const GemmDesc &g) {
+  if (g.K == 0) return 0;
   const Fp4Plan p = plan_fp4(g);
   if (p.ok) return fp4_tiled_encodable(g, p) ? fp4_b_layout(p).total : 0;
   if (int_workspace(g)) return 0;  // integer operands: encoded per call
@@ -631,6 +633,7 @@ int launch_fast_encoded(const GemmDesc &g, const void *benc, size_t enc_bytes, v
 }
 
 int launch_fast(const GemmDesc &g, void *workspace, size_t workspace_bytes, cudaStream_t s, const void *benc) {
+  if (g.K == 0) return TC_UNSUPPORTED;  // bias-only outputs: the generic kernel
   Fp4Plan p = plan_fp4(g);
   if (!p.ok) {
     int st = launch_int(g, workspace, workspace_bytes, s);
