@@ -395,13 +395,12 @@ __global__ void __launch_bounds__(256) tensor_stats_kernel(const void *__restric
     }
     done = n4 << 2;
   } else if (vec) {
-    int64_t n8 = n >> 3;
-    for (int64_t i = tid; i < n8; i += stride) {
-      uint4 u = reinterpret_cast<const uint4 *>(x)[i];
-      uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    const int64_t n8 = n >> 3;
+    auto add8 = [&](const uint4 &u) {
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        uint16_t lo = (uint16_t)(w[j] & 0xFFFF), hi = (uint16_t)(w[j] >> 16);
+        const uint16_t lo = (uint16_t)(w[j] & 0xFFFF), hi = (uint16_t)(w[j] >> 16);
         if (dt == TC_BF16) {
           tstat_add<AMAX_ONLY>(s, u2f((uint32_t)lo << 16));
           tstat_add<AMAX_ONLY>(s, u2f((uint32_t)hi << 16));
@@ -410,7 +409,18 @@ __global__ void __launch_bounds__(256) tensor_stats_kernel(const void *__restric
           tstat_add<AMAX_ONLY>(s, __half2float(__ushort_as_half(hi)));
         }
       }
+    };
+    // Four independent 16-byte loads in flight per thread, then the grid-stride remainder.
+    const uint4 *x8 = reinterpret_cast<const uint4 *>(x);
+    int64_t i = tid;
+    for (; i + 3 * stride < n8; i += 4 * stride) {
+      const uint4 u0 = x8[i], u1 = x8[i + stride], u2 = x8[i + 2 * stride], u3 = x8[i + 3 * stride];
+      add8(u0);
+      add8(u1);
+      add8(u2);
+      add8(u3);
     }
+    for (; i < n8; i += stride) add8(x8[i]);
     done = n8 << 3;
   }
   for (int64_t i = done + tid; i < n; i += stride) tstat_add<AMAX_ONLY>(s, load_as_float(x, dt, i));
