@@ -979,7 +979,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true", help="skip the slow auxiliary measurements (Triton, cfg3)")
     ap.add_argument("--workload", default="all", choices=["all", "cfg2step", "cfg2gemm", "cfg1", "cfg3", "cfg4", "decode",
-                                                      "triton", "rows", "gdfs_row"],
+                                                      "triton", "rows", "gdfs_row", "sweep"],
                     help="run only that measurement on one GPU (for profiling)")
     ap.add_argument("--cube", type=int, default=0,
                     help="with --workload cfg3: run an M = N = K = CUBE case instead of 8192 (profiling)")
@@ -998,6 +998,13 @@ def main() -> None:
             step, macs, shape, _ = gemm_step("cfg2", dev)
             t = statistics.mean(time_gemm_graphed(step, dev, max(args.steps, 1)))
             print(json.dumps({"workload": "cfg2 GEMM", "shape": list(shape), "ms": t, "gmacs": macs / (t * 1e-3) / 1e9}))
+        elif args.workload == "sweep":  # the cfg5 layer sweep on this GPU
+            from tricast_b200.sweep import SweepConfig, measure_costs, run_sweep
+
+            cfg = SweepConfig()
+            breakdown = {}
+            _, secs = run_sweep(cfg, costs=measure_costs(cfg, dev), breakdown=breakdown)
+            print(json.dumps({"workload": "cfg5 sweep", "secs": secs, "per_rank": breakdown}))
         elif args.workload == "cfg2step":
             step, macs, shape, _ = gemm_step("cfg2", dev)
             t = statistics.mean(time_steps(step, dev, args.steps, args.warmup))
