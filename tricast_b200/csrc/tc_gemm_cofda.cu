@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 4 ? 2 : 1) cofda_kernel(Args
       for (int j = 0; j < 4; ++j)
         em2[q][j] = p.dec ? kZeroPair  // decoupled: c takes no part in the chunk
                           : ((uint32_t)running_exp(c[2 * q][j]) & 0xFFFFu) | ((uint32_t)running_exp(c[2 * q + 1][j]) << 16);
-#pragma unroll 8
+#pragma unroll(sizeof(T) == 4 ? CS : 8)  // fully in fp32 (measured 2 % faster); fp64 would spill
     for (int kk = 0; kk < CS; ++kk) {
       const uint2 ea = *reinterpret_cast<const uint2 *>(&st.ae[kk][ty * 2]);
       const uint4 eb = *reinterpret_cast<const uint4 *>(&st.be[kk][tx * 4]);
@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 4 ? 2 : 1) cofda_kernel(Args
           if ((rare >> (i * 4 + j)) & 1u) tot[i][j] = Acc<T>::running(c[i][j], F, emax[i][j], S[i][j]);
     }
     // Pass 2: exact aligned sum, sign(a) * floor(|(|a| * b) * S|) with b's sign, per product.
-#pragma unroll 4
+#pragma unroll(CS > 8 ? 8 : 4)
     for (int kk = 0; kk < CS; ++kk) {
       T am[4], sg[4], bs[4], mb[4];
       load4<T>(&st.av[kk][ty * 4], am);
