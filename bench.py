@@ -781,7 +781,11 @@ def e2e_pipelined(steppers, host_inputs, dev, steps: int, warmup: int, world: in
     inputs and output) and two pinned host outputs alternate, so step i + 1's upload and step i - 1's
     download overlap step i's compute; the ordering is by CUDA events only. Returns (ms per step over
     the K timed steps, from the first upload's start to the last download's end; H2D bytes per step;
-    D2H bytes per step)."""
+    D2H bytes per step).
+
+    With several ranks every rank needs all of A but the ranks share the host's memory: each uploads
+    only its 1/world row slab of A (and its own slab of B), and one NCCL all-gather over NVLink,
+    ordered on the upload stream, assembles A on every rank before the step reads it."""
     import torch
     import torch.distributed as dist
 
@@ -791,6 +795,14 @@ def e2e_pipelined(steppers, host_inputs, dev, steps: int, warmup: int, world: in
     in_ready = [torch.cuda.Event(), torch.cuda.Event()]
     in_free = [torch.cuda.Event(), torch.cuda.Event()]
     out_free = [torch.cuda.Event(), torch.cuda.Event()]
+    a_host = host_inputs[0]
+    split_a = world > 1 and a_host.shape[0] % world == 0
+    uploads = list(host_inputs)
+    if split_a:
+        rows = a_host.shape[0] // world
+        rank = dist.get_rank()
+        uploads[0] = a_host[rank * rows:(rank + 1) * rows]  # a view of the pinned buffer
+        a_parts = [torch.empty(uploads[0].shape, dtype=a_host.dtype, device=dev) for _ in steppers]
 
     def run(n: int) -> None:
         for i in range(n):
@@ -800,8 +812,13 @@ def e2e_pipelined(steppers, host_inputs, dev, steps: int, warmup: int, world: in
                 up.wait_event(in_free[j])    # step i - 2 is done reading these inputs
                 comp.wait_event(out_free[j])  # and its result has been downloaded
             with torch.cuda.stream(up):
-                for d, h in zip(st.inputs, host_inputs):
-                    d.copy_(h, non_blocking=True)
+                if split_a:
+                    a_parts[j].copy_(uploads[0], non_blocking=True)
+                    st.inputs[1].copy_(uploads[1], non_blocking=True)
+                    dist.all_gather_into_tensor(st.inputs[0], a_parts[j])  # the upload stream waits for it
+                else:
+                    for d, h in zip(st.inputs, uploads):
+                        d.copy_(h, non_blocking=True)
                 in_ready[j].record(up)
             comp.wait_event(in_ready[j])
             out = st()
@@ -822,7 +839,7 @@ def e2e_pipelined(steppers, host_inputs, dev, steps: int, warmup: int, world: in
     end.record(down)
     end.synchronize()
     torch.cuda.synchronize(dev)
-    h2d = sum(h.numel() * h.element_size() for h in host_inputs)
+    h2d = sum(h.numel() * h.element_size() for h in uploads)
     return start.elapsed_time(end) / steps, h2d, steppers[0].out.numel() * steppers[0].out.element_size()
 
 
@@ -927,7 +944,8 @@ def run_b200(args) -> None:
                     "d2h_bytes_per_step": d2h_all,
                     "protocol": "K steps pipelined from pinned host memory: upload, compute and download on three "
                                 "streams with double-buffered inputs and outputs; timed from the first upload to "
-                                "the last download; bytes summed over ranks",
+                                "the last download; bytes summed over ranks; with several ranks each uploads "
+                                "its 1/N row slab of A and A is all-gathered over NVLink",
                     "links_rank0": {k: (round(v, 1) if isinstance(v, float) else v) for k, v in links.items()}},
             "gpu_launches": int(launches),
             "graphs": "each step replays CUDA graphs of its public calls; gpu_launches = the library kernels "
